@@ -1,0 +1,189 @@
+/*
+ * C ABI of tcc-spmm-b200: the fused Y = A x dequant(X_int8) SpMM for B200 (sm_100a).
+ *
+ * Every entry point returns a tcc_status. A nonzero status comes with a message that
+ * tcc_last_error() returns on the same host thread. No C++ exception crosses this
+ * boundary. The C++ drop-in headers (spmm.cuh, format/sw32.h, ...) wrap these functions and turn
+ * the status back into the exception type that the reference API throws.
+ *
+ * Conventions shared with the reference library (Shixg-cnic/tcc_spmm):
+ *   - The caller allocates and owns every device buffer. Device entry points allocate
+ *     nothing and never synchronise; they enqueue work on `stream` and return.
+ *   - Sizes are 32-bit, as in the reference (rows, cols, features, nnz).
+ *   - All device pointers are plain CUDA device addresses; `stream` is a cudaStream_t
+ *     (NULL = legacy default stream).
+ */
+#ifndef TCC_SPMM_B200_H
+#define TCC_SPMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in cuda_runtime.h. */
+typedef struct CUstream_st* tcc_stream_t;
+
+typedef enum tcc_status {
+    TCC_OK = 0,
+    TCC_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+    TCC_OVERFLOW = 2,         /* reference: std::overflow_error    */
+    TCC_CUDA_ERROR = 3,       /* reference: std::runtime_error (checkCuda) */
+    TCC_INTERNAL = 4,         /* any other failure (allocation on the host, ...) */
+    TCC_DEVICE_TIMEOUT = 5    /* a bounded device wait ran out (see tcc_device_status) */
+} tcc_status;
+
+/* Sw32Task, 7 x u32 = 28 bytes (include/format/sw32.h:36-38 in the reference). */
+typedef struct tcc_sw32_task {
+    uint32_t sw, begin, end, partial, mask, chunks, reduceFirst;
+} tcc_sw32_task;
+
+/* Sw32ReduceRange (include/format/sw32.h:39-41). */
+typedef struct tcc_sw32_reduce_range {
+    uint32_t begin, end;
+} tcc_sw32_reduce_range;
+
+/* Sw32DeviceView, byte-compatible (include/format/sw32.h:70-79): nine device pointers
+ * followed by the task count. */
+typedef struct tcc_sw32_device_view {
+    const uint32_t* windowOffsets;
+    const uint32_t* sourceIds;
+    const uint32_t* rowGroupMasks;
+    const uint64_t* sourceMetadata;
+    const float* values;
+    const uint32_t* bucketOffsets;
+    const tcc_sw32_task* tasks;
+    const tcc_sw32_reduce_range* reductions;
+    const uint32_t* partialIds;
+    uint32_t taskCount;
+} tcc_sw32_device_view;
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* tcc_last_error(void);
+
+/* Library version string. */
+const char* tcc_version(void);
+
+/* ---------------------------------------------------------------------------------
+ * Device entry points
+ * --------------------------------------------------------------------------------- */
+
+/* Replaces launchSpmmInt8 (reference include/spmm.cuh:21-23, src/kernel/spmm.cu:17-31).
+ * Y[rows x features] = A x (q * scale), A given by the uploaded SW32 view, packed_x the
+ * packed16 INT8 features [cols x features], scales one float per source row.
+ * features must be 128 or 256 (else TCC_INVALID_ARGUMENT, as the reference throws
+ * std::invalid_argument). partials = partialCount*8*features floats and counters =
+ * ceil(rows/32)*(features/128) u32 (zero before the first use, zero again after each
+ * launch); both may be NULL when partialCount is 0. Every Y element is overwritten.
+ * Launches on distinct workspaces may run concurrently. */
+int tcc_launch_spmm_int8(const tcc_sw32_device_view* matrix, const int8_t* packed_x,
+                         const float* scales, float* output, uint32_t rows, uint32_t cols,
+                         uint32_t features, float* partials, uint32_t* counters,
+                         tcc_stream_t stream);
+
+/* Replaces quantizeFeaturesInt8 (reference include/format/int8_features.cuh:9-10,
+ * src/format/int8_quantize.cu:27-31). Per source row: scale = absmax/127 (1 when the row
+ * is all zero), q = clamp(lrintf(x/scale), -127, 127). Byte-identical to the reference. */
+int tcc_quantize_features_int8(const float* x, int8_t* q, float* scale, uint32_t sources,
+                               uint32_t features, tcc_stream_t stream);
+
+/* Replaces packFeaturesInt8x16 (reference include/format/int8_features.cuh:14-15,
+ * src/format/pack_int8.cu:18-25): every 16-feature tile becomes [q0,q8,q1,q9,...,q7,q15].
+ * features % 16 == 0, packed must not alias q. Byte-identical to the reference. */
+int tcc_pack_features_int8x16(const int8_t* q, int8_t* packed, uint32_t sources,
+                              uint32_t features, tcc_stream_t stream);
+
+/* One-pass quantize + pack: reads x once and writes the packed16 bytes and the scales
+ * that quantizeFeaturesInt8 followed by packFeaturesInt8x16 would write (byte-identical).
+ * No separate reference entry point; it fuses reference src/format/int8_quantize.cu:4-25
+ * and src/format/pack_int8.cu:6-15. features % 16 == 0. */
+int tcc_quantize_pack_features_int8(const float* x, int8_t* packed, float* scale,
+                                    uint32_t sources, uint32_t features, tcc_stream_t stream);
+
+/* Workspace sizing of reference src/device_matrix.cuh:18-28: partial floats
+ * (partialCount*8*features) and counter words (ceil(rows/32)*(features/128), 0 when
+ * partialCount is 0). */
+int tcc_spmm_workspace_size(uint32_t rows, uint32_t partial_count, uint32_t features,
+                            uint64_t* partial_floats, uint64_t* counter_words);
+
+/* Status word written by bounded device waits of the SpMM kernel on the current device:
+ * 0 = no wait ran out since the last reset. Synchronises the device. */
+int tcc_device_status(uint32_t* status, int reset);
+
+/* ---------------------------------------------------------------------------------
+ * Host format construction (no GPU needed)
+ * --------------------------------------------------------------------------------- */
+
+/* Canonical CSR owned by the library (reference include/format/csr.h:7-10). */
+typedef struct tcc_csr tcc_csr;
+
+/* Replaces makeCanonicalCsr (reference include/format/csr.h:23-25,
+ * src/format/csr.cpp:6-40): stable-sort each row by column, sum duplicates in that order,
+ * drop zero sums, reject non-finite values and invalid offsets. */
+int tcc_make_canonical_csr(uint32_t rows, uint32_t cols, uint32_t nnz,
+                           const uint32_t* row_offsets, const uint32_t* source_ids,
+                           const float* values, tcc_csr** out);
+/* Views into a tcc_csr (valid until tcc_csr_free). row_offsets has rows+1 entries. */
+int tcc_csr_arrays(const tcc_csr* csr, uint32_t* rows, const uint32_t** row_offsets,
+                   const uint32_t** source_ids, const float** values, uint64_t* nnz);
+void tcc_csr_free(tcc_csr* csr);
+
+/* Replaces loadMatrixMarket (reference include/format/csr.h:18,
+ * src/format/matrix_market.cpp:30-103): coordinate real/integer/pattern,
+ * general/symmetric, symmetric off-diagonals mirrored, then makeCanonicalCsr. The row count
+ * is available through tcc_csr_arrays; cols receives the column count. File and format
+ * errors return TCC_INTERNAL (the reference throws std::runtime_error). */
+int tcc_load_matrix_market(const char* path, uint32_t* cols, tcc_csr** out);
+
+/* SW32 host format owned by the library (reference include/format/sw32.h:45-62). */
+typedef struct tcc_sw32_host tcc_sw32_host;
+
+typedef struct tcc_sw32_sizes {
+    uint32_t rows, cols, partialCount, bucketed;
+    uint64_t windowOffsets;  /* windows + 1 */
+    uint64_t sourceIds;      /* 8 * panels (== sourceMetadata) */
+    uint64_t rowGroupMasks;  /* panels */
+    uint64_t values;         /* nnz */
+    uint64_t bucketOffsets;  /* 17 * windows, or 0 when not bucketed */
+    uint64_t tasks, reductions, partialIds;
+} tcc_sw32_sizes;
+
+typedef struct tcc_sw32_arrays {
+    const uint32_t* windowOffsets;
+    const uint32_t* sourceIds;
+    const uint32_t* rowGroupMasks;
+    const uint64_t* sourceMetadata;
+    const float* values;
+    const uint32_t* bucketOffsets;
+    const tcc_sw32_task* tasks;
+    const tcc_sw32_reduce_range* reductions;
+    const uint32_t* partialIds;
+} tcc_sw32_arrays;
+
+/* Replaces convertCsrToSw32 (reference include/format/sw32.h:66-67,
+ * src/format/sw32.cpp:69-167) including buildPanelTasks (src/format/sw32.cpp:25-65).
+ * Output arrays are byte-identical to the reference; the conversion runs on `threads`
+ * host threads (0 = all hardware threads). */
+int tcc_convert_csr_to_sw32(uint32_t rows, uint32_t cols, const uint32_t* row_offsets,
+                            const uint32_t* source_ids, const float* values, uint64_t nnz,
+                            int bucket_by_rw_mask, uint32_t threads, tcc_sw32_host** out);
+int tcc_sw32_host_sizes(const tcc_sw32_host* host, tcc_sw32_sizes* sizes);
+int tcc_sw32_host_arrays(const tcc_sw32_host* host, tcc_sw32_arrays* arrays);
+void tcc_sw32_host_free(tcc_sw32_host* host);
+
+/* Multi-GPU sharding (no reference counterpart; the reference is single-GPU): cut the
+ * task array into `parts` contiguous ranges at SW boundaries with balanced estimated cost
+ * (panels, active row-group MMAs and the per-task write-back). bounds gets parts+1 task
+ * indices, bounds[0] = 0 and bounds[parts] = task_count. Every split SW stays on one
+ * part, so its partials, counter and merge are local to one GPU. */
+int tcc_partition_tasks(const tcc_sw32_task* tasks, uint32_t task_count,
+                        const uint32_t* row_group_masks, uint32_t features, uint32_t parts,
+                        uint32_t* bounds);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* TCC_SPMM_B200_H */

@@ -1,0 +1,361 @@
+"""Python mirror of the reference's C++ host API for the SpMM path, over the C ABI.
+
+Reference (Shixg-cnic/tcc_spmm)            this module
+-----------------------------------------  ----------------------------------------------
+makeCanonicalCsr   include/format/csr.h:23  make_canonical_csr
+loadMatrixMarket   include/format/csr.h:18  load_matrix_market
+convertCsrToSw32   include/format/sw32.h:66 convert_csr_to_sw32 (includes buildPanelTasks)
+Sw32HostFormat     include/format/sw32.h:45 Sw32HostFormat
+DeviceMatrix       src/device_matrix.cuh:8  DeviceMatrix (view(), workspace())
+SpmmWorkspace      include/spmm.cuh:10      SpmmWorkspace
+launchSpmmInt8     include/spmm.cuh:21      launch_spmm_int8
+quantizeFeaturesInt8 int8_features.cuh:9    quantize_features_int8
+packFeaturesInt8x16  int8_features.cuh:14   pack_features_int8x16
+
+Errors map to the reference's exception types: std::invalid_argument -> InvalidArgument
+(a ValueError), std::overflow_error -> OverflowError, std::runtime_error (CUDA) ->
+CudaError (a RuntimeError). Device calls only enqueue work on the given stream (default:
+torch's current stream of the output's device) and never synchronise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+from . import _native as N
+
+TCC_OK, TCC_INVALID_ARGUMENT, TCC_OVERFLOW, TCC_CUDA_ERROR, TCC_INTERNAL, TCC_DEVICE_TIMEOUT = range(6)
+NO_PARTIAL = 0xFFFFFFFF
+PADDING_SOURCE = 0xFFFFFFFF
+BUCKET_ORDER = (0, 1, 2, 4, 8, 3, 5, 6, 7, 9, 10, 11, 12, 13, 14, 15)
+TASK_PANEL_LIMIT = 384
+
+
+class InvalidArgument(ValueError):
+    """std::invalid_argument of the reference API."""
+
+
+class CudaError(RuntimeError):
+    """std::runtime_error raised by the reference's checkCuda."""
+
+
+class DeviceTimeout(TimeoutError):
+    """A bounded device wait of the SpMM kernel ran out."""
+
+
+def _check(status: int) -> None:
+    if status == TCC_OK:
+        return
+    message = (N.lib().tcc_last_error() or b"").decode(errors="replace")
+    if status == TCC_INVALID_ARGUMENT:
+        raise InvalidArgument(message)
+    if status == TCC_OVERFLOW:
+        raise OverflowError(message)
+    if status == TCC_CUDA_ERROR:
+        raise CudaError(message)
+    if status == TCC_DEVICE_TIMEOUT:
+        raise DeviceTimeout(message)
+    raise RuntimeError(message)
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(C.POINTER(ctype))
+
+
+def _copy_out(ptr, count: int, dtype) -> np.ndarray:
+    if count == 0 or not ptr:
+        return np.zeros(0, dtype=dtype)
+    nbytes = count * np.dtype(dtype).itemsize
+    buf = (C.c_char * nbytes).from_address(ptr if isinstance(ptr, int) else C.cast(ptr, C.c_void_p).value)
+    return np.frombuffer(buf, dtype=dtype).copy()
+
+
+# --------------------------------------------------------------------------------------------
+# Host side
+# --------------------------------------------------------------------------------------------
+@dataclass
+class CsrMatrix:
+    """Canonical CSR (reference include/format/csr.h:7-10)."""
+
+    rows: int
+    cols: int
+    row_offsets: np.ndarray
+    source_ids: np.ndarray
+    values: np.ndarray
+
+    @property
+    def nnz(self) -> int:
+        return int(self.source_ids.size)
+
+
+def _csr_from_handle(handle: C.c_void_p, cols: int) -> CsrMatrix:
+    lib = N.lib()
+    rows = C.c_uint32()
+    ro, si, va = N.u32p(), N.u32p(), N.f32p()
+    nnz = C.c_uint64()
+    try:
+        _check(lib.tcc_csr_arrays(handle, C.byref(rows), C.byref(ro), C.byref(si), C.byref(va), C.byref(nnz)))
+        return CsrMatrix(rows.value, cols, _copy_out(C.cast(ro, C.c_void_p).value, rows.value + 1, np.uint32),
+                         _copy_out(C.cast(si, C.c_void_p).value, nnz.value, np.uint32),
+                         _copy_out(C.cast(va, C.c_void_p).value, nnz.value, np.float32))
+    finally:
+        lib.tcc_csr_free(handle)
+
+
+def make_canonical_csr(rows: int, cols: int, row_offsets, source_ids, values) -> CsrMatrix:
+    """Validate raw CSR and canonicalise it (reference src/format/csr.cpp:6-40)."""
+    ro, si, va = _u32(row_offsets), _u32(source_ids), _f32(values)
+    if ro.size != rows + 1:
+        raise InvalidArgument("invalid CSR dimensions or offsets")
+    nnz = int(ro[-1]) if ro.size else 0
+    if si.size < nnz or va.size < nnz:
+        raise InvalidArgument("invalid CSR offsets")
+    handle = C.c_void_p()
+    _check(N.lib().tcc_make_canonical_csr(rows, cols, nnz, _ptr(ro, C.c_uint32), _ptr(si, C.c_uint32),
+                                          _ptr(va, C.c_float), C.byref(handle)))
+    return _csr_from_handle(handle, cols)
+
+
+@dataclass
+class MtxMatrix:
+    rows: int
+    cols: int
+    csr: CsrMatrix
+
+
+def load_matrix_market(path: str) -> MtxMatrix:
+    """Read a coordinate Matrix Market file into canonical CSR (reference
+    src/format/matrix_market.cpp:30-103)."""
+    handle = C.c_void_p()
+    cols = C.c_uint32()
+    _check(N.lib().tcc_load_matrix_market(str(path).encode(), C.byref(cols), C.byref(handle)))
+    csr = _csr_from_handle(handle, cols.value)
+    return MtxMatrix(csr.rows, cols.value, csr)
+
+
+TASK_DTYPE = np.dtype([(n, "<u4") for n in ("sw", "begin", "end", "partial", "mask", "chunks", "reduceFirst")])
+REDUCE_DTYPE = np.dtype([("begin", "<u4"), ("end", "<u4")])
+
+
+@dataclass
+class Sw32HostFormat:
+    """Host SW32 format and task plan (reference include/format/sw32.h:45-62)."""
+
+    rows: int
+    cols: int
+    window_offsets: np.ndarray
+    source_ids: np.ndarray
+    row_group_masks: np.ndarray
+    source_metadata: np.ndarray
+    values: np.ndarray
+    bucket_offsets: np.ndarray
+    tasks: np.ndarray
+    reductions: np.ndarray
+    partial_ids: np.ndarray
+    partial_count: int
+
+    @property
+    def windows(self) -> int:
+        return int(self.window_offsets.size - 1)
+
+    @property
+    def panels(self) -> int:
+        return int(self.row_group_masks.size)
+
+    @property
+    def nnz(self) -> int:
+        return int(self.values.size)
+
+    @property
+    def valid_slots(self) -> int:
+        return int(np.count_nonzero(self.source_ids != PADDING_SOURCE))
+
+    def algorithmic_bytes(self, features: int) -> dict:
+        """Bytes one SpMM call must move at minimum under the format (one read of every format
+        array, one F-byte row plus a 4-byte scale per valid slot, one write of Y)."""
+        a_bytes = (4 * self.source_ids.size + 8 * self.source_metadata.size + 4 * self.values.size +
+                   4 * self.row_group_masks.size + 4 * self.bucket_offsets.size + 28 * self.tasks.size +
+                   8 * self.reductions.size + 4 * self.partial_ids.size)
+        x_bytes = self.valid_slots * (features + 4)
+        y_bytes = 4 * self.rows * features
+        return {"a_bytes": int(a_bytes), "x_bytes": int(x_bytes), "y_bytes": int(y_bytes),
+                "total": int(a_bytes + x_bytes + y_bytes),
+                "compulsory": int(a_bytes + 4 * self.cols + self.cols * features + y_bytes),
+                "merge_bytes": int(2 * 4 * 8 * features * self.partial_count)}
+
+
+def convert_csr_to_sw32(rows: int, cols: int, csr: CsrMatrix, bucket_by_rw_mask: bool = True,
+                        threads: int = 0) -> Sw32HostFormat:
+    """Build the SW32 format and, when bucketed, its task plan (reference
+    src/format/sw32.cpp:69-167 and :25-65). Byte-identical output; runs on `threads` host
+    threads (0 = all)."""
+    ro, si, va = _u32(csr.row_offsets), _u32(csr.source_ids), _f32(csr.values)
+    if ro.size != rows + 1 or va.size != si.size:
+        raise InvalidArgument("invalid canonical CSR for source-mask SW32")
+    lib = N.lib()
+    handle = C.c_void_p()
+    _check(lib.tcc_convert_csr_to_sw32(rows, cols, _ptr(ro, C.c_uint32), _ptr(si, C.c_uint32), _ptr(va, C.c_float),
+                                       si.size, int(bool(bucket_by_rw_mask)), threads, C.byref(handle)))
+    try:
+        s, a = N.Sw32Sizes(), N.Sw32Arrays()
+        _check(lib.tcc_sw32_host_sizes(handle, C.byref(s)))
+        _check(lib.tcc_sw32_host_arrays(handle, C.byref(a)))
+        return Sw32HostFormat(
+            rows=s.rows, cols=s.cols,
+            window_offsets=_copy_out(a.windowOffsets, s.windowOffsets, np.uint32),
+            source_ids=_copy_out(a.sourceIds, s.sourceIds, np.uint32),
+            row_group_masks=_copy_out(a.rowGroupMasks, s.rowGroupMasks, np.uint32),
+            source_metadata=_copy_out(a.sourceMetadata, s.sourceIds, np.uint64),
+            values=_copy_out(a.values, s.values, np.float32),
+            bucket_offsets=_copy_out(a.bucketOffsets, s.bucketOffsets, np.uint32),
+            tasks=_copy_out(a.tasks, s.tasks * 7, np.uint32).view(TASK_DTYPE),
+            reductions=_copy_out(a.reductions, s.reductions * 2, np.uint32).view(REDUCE_DTYPE),
+            partial_ids=_copy_out(a.partialIds, s.partialIds, np.uint32),
+            partial_count=s.partialCount)
+    finally:
+        lib.tcc_sw32_host_free(handle)
+
+
+def workspace_size(rows: int, partial_count: int, features: int) -> tuple[int, int]:
+    """(partial floats, counter words) of the reference's workspace contract."""
+    pf, cw = C.c_uint64(), C.c_uint64()
+    _check(N.lib().tcc_spmm_workspace_size(rows, partial_count, features, C.byref(pf), C.byref(cw)))
+    return pf.value, cw.value
+
+
+def partition_tasks(fmt: Sw32HostFormat, features: int, parts: int) -> np.ndarray:
+    """parts+1 task-index bounds of balanced contiguous shards, cut at window boundaries."""
+    bounds = np.zeros(parts + 1, dtype=np.uint32)
+    tasks = np.ascontiguousarray(fmt.tasks)
+    masks = _u32(fmt.row_group_masks)
+    _check(N.lib().tcc_partition_tasks(tasks.ctypes.data_as(C.c_void_p), tasks.size, _ptr(masks, C.c_uint32),
+                                       features, parts, _ptr(bounds, C.c_uint32)))
+    return bounds
+
+
+# --------------------------------------------------------------------------------------------
+# Device side (torch is used for device memory and streams only)
+# --------------------------------------------------------------------------------------------
+def _addr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream_handle(stream, like=None) -> int:
+    if stream is None:
+        import torch
+
+        device = like.device if (like is not None and hasattr(like, "device")) else None
+        return int(torch.cuda.current_stream(device).cuda_stream)
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+@dataclass
+class SpmmWorkspace:
+    """partials: partialCount*8*F floats; counters: ceil(rows/32)*(F/128) u32 (zeroed)."""
+
+    partials: object = None
+    counters: object = None
+
+
+class DeviceMatrix:
+    """Uploads every SW32 array and allocates the split-task workspace for `features`
+    (reference src/device_matrix.cuh:8-37): partials = partialCount*8*F floats, counters =
+    windows*(F/128) zeroed u32 when partialCount > 0."""
+
+    def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None):
+        import torch
+
+        self.rows, self.cols, self.features = fmt.rows, fmt.cols, features
+        self.device = torch.device(device)
+
+        def up(a: np.ndarray, dtype):
+            if a.size == 0:
+                return torch.zeros(1, dtype=dtype, device=self.device)
+            return torch.from_numpy(np.ascontiguousarray(a).view(_np_of(dtype))).to(self.device)
+
+        self.window_offsets = up(fmt.window_offsets, torch.int32)
+        self.source_ids = up(fmt.source_ids, torch.int32)
+        self.row_group_masks = up(fmt.row_group_masks, torch.int32)
+        self.source_metadata = up(fmt.source_metadata, torch.int64)
+        self.values = up(fmt.values, torch.float32)
+        self.bucket_offsets = up(fmt.bucket_offsets, torch.int32)
+        tasks = fmt.tasks if task_range is None else fmt.tasks[task_range[0]:task_range[1]]
+        self.task_count = int(tasks.size)
+        self.tasks = up(np.ascontiguousarray(tasks).view(np.uint32), torch.int32)
+        self.reductions = up(np.ascontiguousarray(fmt.reductions).view(np.uint32), torch.int32)
+        self.partial_ids = up(fmt.partial_ids, torch.int32)
+        self.partial_count = fmt.partial_count
+        pf, cw = workspace_size(fmt.rows, fmt.partial_count, features)
+        self.partials = torch.empty(pf, dtype=torch.float32, device=self.device) if pf else None
+        self.counters = torch.zeros(cw, dtype=torch.int32, device=self.device) if cw else None
+
+    def view(self) -> N.Sw32DeviceView:
+        return N.Sw32DeviceView(self.window_offsets.data_ptr(), self.source_ids.data_ptr(),
+                                self.row_group_masks.data_ptr(), self.source_metadata.data_ptr(),
+                                self.values.data_ptr(), self.bucket_offsets.data_ptr(), self.tasks.data_ptr(),
+                                self.reductions.data_ptr(), self.partial_ids.data_ptr(), self.task_count)
+
+    def workspace(self) -> SpmmWorkspace:
+        return SpmmWorkspace(self.partials, self.counters)
+
+    def nbytes(self) -> int:
+        ts = [self.window_offsets, self.source_ids, self.row_group_masks, self.source_metadata, self.values,
+              self.bucket_offsets, self.tasks, self.reductions, self.partial_ids, self.partials, self.counters]
+        return sum(t.numel() * t.element_size() for t in ts if t is not None)
+
+
+def _np_of(torch_dtype):
+    import torch
+
+    return {torch.int32: np.int32, torch.int64: np.int64, torch.float32: np.float32}[torch_dtype]
+
+
+def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,
+                     workspace: Optional[SpmmWorkspace] = None, stream=None, generic: bool = False) -> None:
+    """Y = A x dequant(packed_x) (reference include/spmm.cuh:21-23). Asynchronous on `stream`."""
+    ws = workspace or SpmmWorkspace()
+    fn = N.lib().tcc_launch_spmm_int8_generic if generic else N.lib().tcc_launch_spmm_int8
+    _check(fn(C.byref(view), _addr(packed_x), _addr(scales), _addr(output), rows, cols, features,
+              _addr(ws.partials), _addr(ws.counters), _stream_handle(stream, output)))
+
+
+def quantize_features_int8(x, q, scale, sources: int, features: int, stream=None) -> None:
+    """Per-row absmax INT8 quantization (reference src/format/int8_quantize.cu:27-31)."""
+    _check(N.lib().tcc_quantize_features_int8(_addr(x), _addr(q), _addr(scale), sources, features,
+                                              _stream_handle(stream, q)))
+
+
+def pack_features_int8x16(q, packed, sources: int, features: int, stream=None) -> None:
+    """packed16 interleave (reference src/format/pack_int8.cu:18-25)."""
+    _check(N.lib().tcc_pack_features_int8x16(_addr(q), _addr(packed), sources, features,
+                                             _stream_handle(stream, packed)))
+
+
+def quantize_pack_features_int8(x, packed, scale, sources: int, features: int, stream=None) -> None:
+    """One-pass quantize + pack; same bytes as quantize_features_int8 then pack_features_int8x16."""
+    _check(N.lib().tcc_quantize_pack_features_int8(_addr(x), _addr(packed), _addr(scale), sources, features,
+                                                   _stream_handle(stream, packed)))
+
+
+def device_status(reset: bool = False) -> int:
+    """Status word of bounded device waits (0 = none ran out). Synchronises the device."""
+    st = C.c_uint32()
+    _check(N.lib().tcc_device_status(C.byref(st), int(reset)))
+    return st.value

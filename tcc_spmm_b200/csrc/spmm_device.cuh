@@ -1,0 +1,136 @@
+// Device helpers of the SpMM kernels: TF32 operand preparation, the m16n8k8 TF32 MMA,
+// packed f32x2 arithmetic, mbarriers and asynchronous copies (sm_100a inline PTX).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tcc {
+namespace dev {
+
+// ---- TF32 operands ----------------------------------------------------------------------
+// The reference rounds both MMA operands with cvt.rna.tf32.f32 (round to 10 mantissa bits,
+// ties away from zero; reference src/kernel/spmm_kernel.cuh:7-11). Adding half a TF32 ulp
+// (0x1000) to the FP32 bit pattern and dropping the low 13 bits is the same rounding for
+// finite values: the carry out of the kept bits implements "half away from zero" on the
+// magnitude. The tensor core ignores the low 13 bits of a TF32 operand, so the hot loop only
+// adds; tf32Exact also clears them (used where the value is stored or compared).
+__device__ __forceinline__ uint32_t tf32Biased(float v) { return __float_as_uint(v) + 0x1000u; }
+__device__ __forceinline__ uint32_t tf32Exact(float v) {
+    return (__float_as_uint(v) + 0x1000u) & 0xFFFFE000u;
+}
+
+// D(16x8) += A(16x8, row-major) * B(8x8, column-major), TF32 inputs, FP32 accumulate.
+__device__ __forceinline__ void mmaTf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- packed FP32 pairs (sm_100a add/mul .f32x2) -----------------------------------------
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t lo32(unsigned long long v) { return static_cast<uint32_t>(v); }
+__device__ __forceinline__ uint32_t hi32(unsigned long long v) { return static_cast<uint32_t>(v >> 32); }
+
+// Dequantize the four INT8 features of one 32-bit word of a source row to biased TF32:
+// out[i] = tf32(float(q_i) * scale). The signed byte is flipped to an unsigned one
+// (q + 128), placed in the mantissa of 2^23 (exact float 2^23 + q + 128) and the offset is
+// subtracted exactly, so float(q_i) costs one byte permute and half a packed add. The
+// product is one IEEE multiply like the reference's float(int8) * multiplier.
+__device__ __forceinline__ void dequant4(uint32_t word, unsigned long long scale2, uint32_t (&out)[4]) {
+    const uint32_t w = word ^ 0x80808080u;
+    const uint32_t magic = 0x4B000000u;
+    const unsigned long long bias2 = 0xCB000080CB000080ull; // (-8388736.f, -8388736.f)
+    const unsigned long long p01 =
+        (static_cast<unsigned long long>(__byte_perm(w, magic, 0x7541)) << 32) | __byte_perm(w, magic, 0x7540);
+    const unsigned long long p23 =
+        (static_cast<unsigned long long>(__byte_perm(w, magic, 0x7543)) << 32) | __byte_perm(w, magic, 0x7542);
+    const unsigned long long f01 = mul2(add2(p01, bias2), scale2);
+    const unsigned long long f23 = mul2(add2(p23, bias2), scale2);
+    out[0] = lo32(f01) + 0x1000u;
+    out[1] = hi32(f01) + 0x1000u;
+    out[2] = lo32(f23) + 0x1000u;
+    out[3] = hi32(f23) + 0x1000u;
+}
+
+// ---- shared memory, mbarriers, async copies ----------------------------------------------
+__device__ __forceinline__ uint32_t smemAddr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbarInit(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbarArrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbarExpectTx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbarTryWait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done)
+                 : "r"(bar), "r"(parity)
+                 : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ uint64_t globalTimerNs() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Arrive on `bar` once every cp.async issued so far by this thread has landed. The barrier's
+// expected count includes this arrival.
+__device__ __forceinline__ void cpAsyncArriveNoinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// 4-byte async copy; srcBytes 0 writes zero.
+__device__ __forceinline__ void cpAsync4(uint32_t dst, const void* src, uint32_t srcBytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(srcBytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cpAsync8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpAsyncWaitAll() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Bulk (TMA engine) copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing as transaction bytes on `bar`. No
+// multicast: every copy lands in the issuing CTA only.
+__device__ __forceinline__ void bulkCopyG2S(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void fenceBarrierInit() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Ticket of the in-kernel merge: atomically increments *counter, wrapping to 0 after
+// `bound` (so the last of bound+1 arrivals resets it), with acquire-release ordering at GPU
+// scope. Same primitive as the reference (src/kernel/spmm_kernel.cuh:257-260).
+__device__ __forceinline__ uint32_t ticketIncrement(uint32_t* counter, uint32_t bound) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(counter), "r"(bound) : "memory");
+    return old;
+}
+
+} // namespace dev
+} // namespace tcc

@@ -1,0 +1,80 @@
+"""The C ABI library loads, exports every function that include/*.h declares, and rejects
+bad arguments with the reference's error types before touching the GPU."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import tcc_spmm_b200 as T
+import tcc_spmm_b200._native as N
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared(header: Path) -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+    return set(re.findall(r"\b(tcc_[a-z0-9_]+)\s*\(", text))
+
+
+def test_every_declared_function_is_exported(native):
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        names |= _declared(header)
+    assert "tcc_launch_spmm_int8" in names and len(names) >= 15
+    missing = [n for n in sorted(names) if not hasattr(native, n)]
+    assert not missing, f"not exported: {missing}"
+    assert set(names) <= set(N.SIGNATURES), "ctypes signatures out of date"
+
+
+def test_cpp_drop_in_symbols_exported():
+    out = subprocess.run(["nm", "-DC", "--defined-only", str(N.library_path())], capture_output=True, text=True,
+                         check=True).stdout
+    for sig in ("launchSpmmInt8(Sw32DeviceView", "quantizeFeaturesInt8(float const*", "packFeaturesInt8x16(",
+                "convertCsrToSw32(unsigned int, unsigned int, CsrMatrix const&, bool)", "makeCanonicalCsr(",
+                "loadMatrixMarket("):
+        assert sig in out, sig
+
+
+def test_abi_struct_sizes():
+    assert C.sizeof(N.Sw32Task) == 28
+    assert C.sizeof(N.Sw32DeviceView) == 9 * 8 + 8
+    assert T.api.TASK_DTYPE.itemsize == 28
+
+
+def test_errors_before_any_device_work(native):
+    view = N.Sw32DeviceView()
+    view.taskCount = 1
+    # features outside {128, 256}: std::invalid_argument in the reference (spmm.cu:28)
+    assert native.tcc_launch_spmm_int8(C.byref(view), 16, 16, 16, 1, 1, 64, None, None, None) == 1
+    assert b"128 or 256" in native.tcc_last_error()
+    with pytest.raises(T.InvalidArgument):
+        T.launch_spmm_int8(view, 16, 16, 16, 1, 1, 200, stream=0)
+    assert native.tcc_pack_features_int8x16(16, 32, 4, 8, None) == 1  # features % 16
+    pf, cw = T.workspace_size(100, 3, 256)
+    assert (pf, cw) == (3 * 8 * 256, 4 * 2)
+    assert T.workspace_size(100, 0, 128) == (0, 0)
+    with pytest.raises(T.InvalidArgument):
+        T.workspace_size(100, 1, 96)
+
+
+def test_version_string(native):
+    assert b"sm_100a" in native.tcc_version()
+
+
+def test_partition_keeps_split_windows_whole():
+    from tcc_spmm_b200 import workloads as W
+
+    csr = W.generate("stress_small")
+    fmt = T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+    for parts in (1, 2, 3, 4, 8):
+        b = T.partition_tasks(fmt, 128, parts)
+        assert b[0] == 0 and b[-1] == fmt.tasks.size and np.all(np.diff(b.astype(np.int64)) >= 0)
+        sw = fmt.tasks["sw"]
+        for k in b[1:-1]:
+            if 0 < k < sw.size:
+                assert sw[k] != sw[k - 1], "a split window was cut"

@@ -1,0 +1,150 @@
+"""SpMM parity on the B200 through the C ABI: Y within the reference's TF32 bound of the CPU
+oracle (and of the reference kernel itself), bit-exact where Y is a single TF32 product,
+counters back to zero, repeated launches identical, no writes outside Y and the workspace."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+import tcc_spmm_b200 as T
+from tcc_spmm_b200 import workloads as W
+from tests.cases import EDGE_CASES, random_csr
+from tests.conftest import assert_within_tf32_bound
+from tests.gpu_util import build_case, oracle_y, run_spmm
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+@pytest.mark.parametrize("generic", [False, True], ids=["pipelined", "generic"])
+@pytest.mark.parametrize("features", [128, 256])
+@pytest.mark.parametrize("name", sorted(EDGE_CASES))
+def test_edge_cases_within_tf32_bound(name, features, generic):
+    torch = _torch()
+    case = build_case(EDGE_CASES[name](), features)
+    y = run_spmm(case, generic=generic)
+    torch.cuda.synchronize()
+    y_ref, bound = oracle_y(case)
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all(), "every Y element must be written"
+    assert_within_tf32_bound(got, y_ref, bound, f"{name}/F{features}")
+    if case.dm.counters is not None:
+        assert int(case.dm.counters.abs().sum()) == 0, "counters must return to zero"
+
+
+@pytest.mark.parametrize("features", [128, 256])
+@pytest.mark.parametrize("name", ["cpu4096", "powerlaw_small", "stress_small", "rmat_small"])
+def test_seeded_configs_within_tf32_bound(name, features):
+    torch = _torch()
+    case = build_case(W.generate(name), features, seed=7)
+    y = run_spmm(case)
+    torch.cuda.synchronize()
+    y_ref, bound = oracle_y(case)
+    assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, f"{name}/F{features}")
+
+
+@pytest.mark.parametrize("generic", [False, True], ids=["pipelined", "generic"])
+def test_single_term_rows_bit_exact(generic):
+    """One nonzero per row: Y = tf32_rna(a) * tf32_rna(q*s) exactly, which pins the operand
+    rounding (round-half-away on 10 mantissa bits) on the tensor cores."""
+    torch = _torch()
+    case = build_case(EDGE_CASES["single_term"](), 128, seed=11)
+    y = run_spmm(case, generic=generic)
+    torch.cuda.synchronize()
+    y_ref, _ = oracle_y(case)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), y_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("features", [128, 256])
+def test_repeated_launches_identical_and_counters_reset(features):
+    torch = _torch()
+    case = build_case(W.generate("stress_small"), features, seed=3)
+    assert case.fmt.partial_count > 0
+    stream = torch.cuda.Stream()  # non-default, non-blocking stream
+    with torch.cuda.stream(stream):
+        y1 = run_spmm(case, stream=stream)
+        y2 = run_spmm(case, stream=stream)
+    stream.synchronize()
+    assert torch.equal(y1.view(torch.int32), y2.view(torch.int32))
+    assert int(case.dm.counters.abs().sum()) == 0
+
+
+def test_generic_and_pipelined_agree_within_bound():
+    torch = _torch()
+    case = build_case(W.generate("powerlaw_small"), 128, seed=5)
+    a = run_spmm(case)
+    b = run_spmm(case, generic=True)
+    torch.cuda.synchronize()
+    _, bound = oracle_y(case)
+    assert_within_tf32_bound(a.cpu().numpy(), b.cpu().numpy(), 2 * bound, "pipelined vs generic")
+
+
+def test_no_writes_outside_outputs():
+    """Canary words around Y and the partial workspace stay untouched."""
+    torch = _torch()
+    case = build_case(W.generate("stress_small"), 128, seed=9)
+    rows, F = case.fmt.rows, 128
+    pad = 4096
+    canary = -7.77e30
+    big = torch.full((rows * F + 2 * pad,), canary, device="cuda")
+    y = big[pad:pad + rows * F].view(rows, F)
+    pf = case.dm.partials.numel()
+    pbig = torch.full((pf + 2 * pad,), canary, device="cuda")
+    case.dm.partials = pbig[pad:pad + pf]
+    run_spmm(case, out=y)
+    torch.cuda.synchronize()
+    for buf in (big, pbig):
+        assert bool((buf[:pad] == canary).all()) and bool((buf[-pad:] == canary).all())
+
+
+def test_misaligned_packed_x_uses_generic_path():
+    torch = _torch()
+    case = build_case(random_csr(500, 700, 8.0, 4), 128, seed=2)
+    raw = torch.empty(case.packed_dev.numel() + 2, dtype=torch.int8, device="cuda")
+    shifted = raw[2:]
+    shifted.copy_(case.packed_dev)
+    case.packed_dev = shifted  # 2-byte aligned only
+    y = run_spmm(case)
+    torch.cuda.synchronize()
+    y_ref, bound = oracle_y(case)
+    assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, "misaligned packedX")
+
+
+def test_bad_feature_count_raises_invalid_argument():
+    torch = _torch()
+    case = build_case(random_csr(64, 64, 4.0, 1), 128)
+    y = torch.empty(64, 128, device="cuda")
+    with pytest.raises(T.InvalidArgument, match="128 or 256"):
+        T.launch_spmm_int8(case.dm.view(), case.packed_dev, case.scales_dev, y, 64, 64, 64, case.dm.workspace())
+
+
+@pytest.mark.skipif(not O.have_ref_cuda("sm100a"), reason="reference kernel not built")
+@pytest.mark.parametrize("tag", ["sm100a", "sm80"])
+@pytest.mark.parametrize("features", [128, 256])
+def test_matches_reference_kernel(tag, features):
+    """The reference's own kernel on the same inputs (second oracle)."""
+    torch = _torch()
+    if not O.have_ref_cuda(tag):
+        pytest.skip(f"reference {tag} build missing")
+    ref = O.ref_cuda(tag)
+    case = build_case(W.generate("stress_small"), features, seed=13)
+    y = run_spmm(case)
+    y_ref = torch.full_like(y, float("nan"))
+    view = case.dm.view()
+    import ctypes
+
+    ws = case.dm.workspace()
+    ref.launch_spmm_int8(ctypes.addressof(view), case.packed_dev.data_ptr(), case.scales_dev.data_ptr(),
+                         y_ref.data_ptr(), case.fmt.rows, case.fmt.cols, features,
+                         ws.partials.data_ptr() if ws.partials is not None else 0,
+                         ws.counters.data_ptr() if ws.counters is not None else 0,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    _, bound = oracle_y(case)
+    assert_within_tf32_bound(y.cpu().numpy(), y_ref.cpu().numpy(), bound, f"reference {tag}")
