@@ -50,7 +50,8 @@ def parse_args():
     p.add_argument("--impl", default="tcc", choices=["tcc", "reference"])
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--generic", action="store_true", help="time the generic (non-pipelined) kernel")
+    p.add_argument("--variant", default="default", choices=["default", "generic", "persistent32", "persistent64"],
+                   help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()
 
@@ -258,7 +259,7 @@ def run_tcc(args):
     view, ws = dm.view(), dm.workspace()
 
     def launch():
-        T.launch_spmm_int8(view, packed, scales, y, fmt.rows, fmt.cols, F, ws, stream=stream, generic=args.generic)
+        T.launch_spmm_int8(view, packed, scales, y, fmt.rows, fmt.cols, F, ws, stream=stream, variant=args.variant)
 
     def barrier():
         if world > 1:
@@ -353,7 +354,7 @@ def run_tcc(args):
                    "features": F, "panels": fmt.panels, "valid_slots": full["x_bytes"] // (F + 4),
                    "tasks": int(fmt.tasks.size), "partial_count": fmt.partial_count,
                    "parallelism": f"task-range shards x{world}, X replicated, Y rows per rank",
-                   "l2": "inputs larger than L2 (no flush)", "kernel": "generic" if args.generic else "pipelined",
+                   "l2": "inputs larger than L2 (no flush)", "kernel": args.variant,
                    "prep": prep},
         "hbm_gbs_alg": round(full["total"] / (ms_step / 1e3) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

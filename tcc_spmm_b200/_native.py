@@ -86,9 +86,9 @@ SIGNATURES = {
     "tcc_version": (C.c_char_p, []),
     "tcc_launch_spmm_int8": (C.c_int, [C.POINTER(Sw32DeviceView), C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
                                        C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),
-    "tcc_launch_spmm_int8_generic": (C.c_int, [C.POINTER(Sw32DeviceView), C.c_void_p, C.c_void_p, C.c_void_p,
+    "tcc_launch_spmm_int8_variant": (C.c_int, [C.POINTER(Sw32DeviceView), C.c_void_p, C.c_void_p, C.c_void_p,
                                                C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p,
-                                               C.c_void_p]),
+                                               C.c_void_p, C.c_int]),
     "tcc_quantize_features_int8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "tcc_pack_features_int8x16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "tcc_quantize_pack_features_int8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,

@@ -327,13 +327,23 @@ def _np_of(torch_dtype):
     return {torch.int32: np.int32, torch.int64: np.int64, torch.float32: np.float32}[torch_dtype]
 
 
+KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3}
+
+
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,
-                     workspace: Optional[SpmmWorkspace] = None, stream=None, generic: bool = False) -> None:
-    """Y = A x dequant(packed_x) (reference include/spmm.cuh:21-23). Asynchronous on `stream`."""
+                     workspace: Optional[SpmmWorkspace] = None, stream=None, generic: bool = False,
+                     variant: str = "default") -> None:
+    """Y = A x dequant(packed_x) (reference include/spmm.cuh:21-23). Asynchronous on `stream`.
+    `variant`/`generic` pick a kernel explicitly (tests and tuning); the default is what
+    launchSpmmInt8 runs."""
     ws = workspace or SpmmWorkspace()
-    fn = N.lib().tcc_launch_spmm_int8_generic if generic else N.lib().tcc_launch_spmm_int8
-    _check(fn(C.byref(view), _addr(packed_x), _addr(scales), _addr(output), rows, cols, features,
-              _addr(ws.partials), _addr(ws.counters), _stream_handle(stream, output)))
+    args = (C.byref(view), _addr(packed_x), _addr(scales), _addr(output), rows, cols, features, _addr(ws.partials),
+            _addr(ws.counters), _stream_handle(stream, output))
+    v = KERNEL_VARIANTS["generic"] if generic else KERNEL_VARIANTS[variant]
+    if v == 0:
+        _check(N.lib().tcc_launch_spmm_int8(*args))
+    else:
+        _check(N.lib().tcc_launch_spmm_int8_variant(*args, v))
 
 
 def quantize_features_int8(x, q, scale, sources: int, features: int, stream=None) -> None:

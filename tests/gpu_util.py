@@ -48,12 +48,12 @@ def build_case(csr: T.CsrMatrix, features: int, seed: int = 1, device: str = "cu
     return Case(fmt, dm, features, x, q, s, packed, scales)
 
 
-def run_spmm(case: Case, generic: bool = False, stream=None, out=None):
+def run_spmm(case: Case, variant: str = "default", stream=None, out=None):
     import torch
 
     y = out if out is not None else torch.full((case.fmt.rows, case.features), float("nan"), device=case.dm.device)
     T.launch_spmm_int8(case.dm.view(), case.packed_dev, case.scales_dev, y, case.fmt.rows, case.fmt.cols,
-                       case.features, case.dm.workspace(), stream=stream, generic=generic)
+                       case.features, case.dm.workspace(), stream=stream, variant=variant)
     return y
 
 

@@ -22,13 +22,13 @@ def _torch():
     return torch
 
 
-@pytest.mark.parametrize("generic", [False, True], ids=["pipelined", "generic"])
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64"])
 @pytest.mark.parametrize("features", [128, 256])
 @pytest.mark.parametrize("name", sorted(EDGE_CASES))
-def test_edge_cases_within_tf32_bound(name, features, generic):
+def test_edge_cases_within_tf32_bound(name, features, variant):
     torch = _torch()
     case = build_case(EDGE_CASES[name](), features)
-    y = run_spmm(case, generic=generic)
+    y = run_spmm(case, variant=variant)
     torch.cuda.synchronize()
     y_ref, bound = oracle_y(case)
     got = y.cpu().numpy()
@@ -49,13 +49,13 @@ def test_seeded_configs_within_tf32_bound(name, features):
     assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, f"{name}/F{features}")
 
 
-@pytest.mark.parametrize("generic", [False, True], ids=["pipelined", "generic"])
-def test_single_term_rows_bit_exact(generic):
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64"])
+def test_single_term_rows_bit_exact(variant):
     """One nonzero per row: Y = tf32_rna(a) * tf32_rna(q*s) exactly, which pins the operand
     rounding (round-half-away on 10 mantissa bits) on the tensor cores."""
     torch = _torch()
     case = build_case(EDGE_CASES["single_term"](), 128, seed=11)
-    y = run_spmm(case, generic=generic)
+    y = run_spmm(case, variant=variant)
     torch.cuda.synchronize()
     y_ref, _ = oracle_y(case)
     assert np.array_equal(y.cpu().numpy().view(np.uint32), y_ref.view(np.uint32))
@@ -79,7 +79,7 @@ def test_generic_and_pipelined_agree_within_bound():
     torch = _torch()
     case = build_case(W.generate("powerlaw_small"), 128, seed=5)
     a = run_spmm(case)
-    b = run_spmm(case, generic=True)
+    b = run_spmm(case, variant="generic")
     torch.cuda.synchronize()
     _, bound = oracle_y(case)
     assert_within_tf32_bound(a.cpu().numpy(), b.cpu().numpy(), 2 * bound, "pipelined vs generic")
