@@ -50,7 +50,8 @@ def parse_args():
     p.add_argument("--impl", default="tcc", choices=["tcc", "reference"])
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--variant", default="default", choices=["default", "generic", "persistent32", "persistent64"],
+    p.add_argument("--variant", default="default",
+                   choices=["default", "generic", "persistent32", "persistent64"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()

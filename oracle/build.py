@@ -76,6 +76,38 @@ def build_reference(force: bool = False) -> bool:
     return True
 
 
+def build_dropin(force: bool = False) -> bool:
+    """The reference's own CLI driver (src/main.cu + src/device_matrix.cuh, unmodified) built
+    twice into oracle/_ref:
+      tcc_spmm_run_ref     against the reference library (all reference sources, sm_100a)
+      tcc_spmm_run_dropin  against this repository's headers (include/) and
+                           libtcc_spmm_b200.so - the drop-in check: the reference's caller
+                           compiles and links unchanged against the new library."""
+    if not reference_present():
+        return False
+    repo = HERE.parent
+    lib = repo / "tcc_spmm_b200" / "_lib" / "libtcc_spmm_b200.so"
+    if not lib.exists():
+        return False
+    REF_OUT.mkdir(exist_ok=True)
+    main = REFERENCE / "src/main.cu"
+    ref_bin = REF_OUT / "tcc_spmm_run_ref"
+    srcs = [main, REFERENCE / "src/format/sw32.cpp", REFERENCE / "src/format/csr.cpp",
+            REFERENCE / "src/format/matrix_market.cpp", REFERENCE / "src/format/int8_quantize.cu",
+            REFERENCE / "src/format/pack_int8.cu", REFERENCE / "src/kernel/spmm.cu"]
+    if force or _stale(ref_bin, srcs):
+        _run([NVCC, "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-I", REFERENCE / "include",
+              "-I", REFERENCE / "src", "-I", REFERENCE / "src/kernel", "-x", "cu", *srcs, "-o", ref_bin])
+    dropin = REF_OUT / "tcc_spmm_run_dropin"
+    if force or _stale(dropin, [main, lib, *sorted((repo / "include").rglob("*.h*"))]):
+        # Only the repository's include/ precedes the reference's src/ (which holds nothing but
+        # main.cu and device_matrix.cuh), so every library header comes from this repository.
+        _run([NVCC, "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-I", repo / "include", "-I",
+              REFERENCE / "src", main, "-L", lib.parent, "-ltcc_spmm_b200", "-Xlinker",
+              "-rpath=$ORIGIN/../../tcc_spmm_b200/_lib", "-o", dropin])
+    return True
+
+
 if __name__ == "__main__":
     force = "--force" in sys.argv
     build_oracle(force)

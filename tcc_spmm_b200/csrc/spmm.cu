@@ -65,16 +65,18 @@ void launchPersistent(const tcc_sw32_device_view& m, const int8_t* x, const floa
         m, x, scales, y, rows, cols, partials, counters);
 }
 
-// variant: 0 = default fast path, 1 = generic kernel, 2 = persistent with 32-feature
-// consumers, 3 = persistent with 64-feature consumers.
+// variant: 0 = default fast path, 1 = generic kernel, 2/3 = persistent kernel with 32/64
+// features per consumer warp.
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
+    if (variant == 0)
+        variant = F == 128 ? 2 : 3;
     if (variant == 1 || !fast) {
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,
                                                                              counters);
-    } else if (variant == 2 || (variant == 0 && F == 128)) {
+    } else if (variant == 2) {
         launchPersistent<F, 32>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else {
         launchPersistent<F, 64>(m, x, scales, y, rows, cols, partials, counters, stream);

@@ -106,6 +106,40 @@ __device__ __forceinline__ void cpAsync4(uint32_t dst, const void* src, uint32_t
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(srcBytes)
                  : "memory");
 }
+// 16-byte async copy through L2 only (no L1 allocation); srcBytes 0 writes zeros.
+__device__ __forceinline__ void cpAsync16(uint32_t dst, const void* src, uint32_t srcBytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(srcBytes) : "memory");
+}
+// L2 eviction policies (createpolicy): keep the gathered feature rows, stream the format.
+__device__ __forceinline__ uint64_t policyEvictLast() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policyEvictFirst() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// 16-byte async copy with an L2 policy and a 128-byte L2 prefetch of the enclosing line.
+__device__ __forceinline__ void cpAsync16Hint(uint32_t dst, const void* src, uint32_t srcBytes, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint.L2::128B [%0], [%1], 16, %2, %3;" ::"r"(dst), "l"(src),
+                 "r"(srcBytes), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void cpAsync4Hint(uint32_t dst, const void* src, uint32_t srcBytes, uint64_t policy) {
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2, %3;" ::"r"(dst), "l"(src), "r"(srcBytes),
+                 "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void cpAsync8Hint(uint32_t dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, 8, %2;" ::"r"(dst), "l"(src), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void cpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cpAsyncWaitGroup() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void cpAsync8(uint32_t dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }

@@ -2,29 +2,31 @@
 //
 // Grid: one CTA per resident slot (SMs x occupancy). CTA b processes tasks b, b+G, b+2G, ...
 // (G = grid size), so at any moment the CTAs of the GPU work on neighbouring 32-row windows
-// and the X rows they share stay in L2. Each CTA covers ALL feature slices of its tasks, so
-// the SW32 arrays are read once per call at F=256 too.
+// and the feature rows they share stay in L2. Each CTA covers ALL feature slices of its tasks,
+// so the SW32 arrays are read once per call at F=256 too.
 //
-// Warp NC (producer) streams the 4-panel chunks of all the CTA's tasks through three
-// asynchronous stages; nothing it does waits on a copy it issued less than several chunks
-// earlier:
-//   A step  (kALead chunks ahead): cp.async of the chunk's 32 source IDs, 32 metadata words
-//           and 4 row-group masks into the A ring.
-//   VX step (kVLead chunks ahead): once the A data has landed and the X stage is free: one
-//           cp.async.bulk (TMA engine, no multicast) per valid slot gathers the F-byte
-//           packed16 source row into the stage, cp.async brings its scale (zero for padding
-//           slots), and the chunk's contiguous value range is copied into the V ring.
-//   F step  (the current chunk): once the values have landed, the TF32-rounded A values are
-//           scattered into m16n8k8 B-fragment order for the chunk's active 8-row groups and
-//           the stage is published (mbarrier arrive with release semantics).
-// Warps 0..NC-1 (consumers) own FPW features each. Per panel they read their 4 or 8 bytes of
-// each of two source rows with one conflict-free shared load each (rows are skewed by 32
-// bytes), dequantize in registers (byte permute into the mantissa of 2^23, packed f32x2
+// The chunks (4 panels = 32 source slots) of all the CTA's tasks form one stream that three
+// roles work through at different distances:
+//   producer warp, A step  (kALead chunks ahead): cp.async of the chunk's 32 source IDs,
+//       32 metadata words and 4 row-group masks into the A ring (L2 evict-first: the format is
+//       read once).
+//   producer warp, V step  (kVLead chunks ahead): cp.async of the chunk's contiguous value
+//       range and of its 32 scales into the V ring.
+//   consumer warps, X step (kPrefetch chunks ahead): every consumer warp gathers its own
+//       FPW-byte slice of the chunk's 32 packed16 source rows with 16-byte cp.async (L2
+//       evict-last plus a 128-byte L2 prefetch: the rows are reused by neighbouring windows),
+//       tracked by its own cp.async groups.
+//   producer warp, F step  (the chunk to be consumed next): the TF32-rounded A values are
+//       scattered into m16n8k8 B-fragment order for the chunk's active 8-row groups, the
+//       scales into (s_t, s_t+4) pair order, and the stage is published (mbarrier arrive with
+//       release semantics).
+// Consumers then read their bytes of two source rows per panel with one conflict-free shared
+// load each, dequantize in registers (byte permute into the mantissa of 2^23, packed f32x2
 // subtract and multiply, +half-ulp TF32 rounding) and issue FPW/16 m16n8k8 TF32 MMAs per
 // active 8-row group into register accumulators. At a task boundary they write Y directly
 // from the fragments (or the task's partial blocks, followed by the last-arriver merge,
-// reference src/kernel/spmm_kernel.cuh:228-282) while the producer already streams the next
-// task.
+// reference src/kernel/spmm_kernel.cuh:228-282) while the producer streams the next task.
+// Every mbarrier wait is bounded (about two seconds).
 #pragma once
 #include "spmm_common.cuh"
 
@@ -36,29 +38,36 @@ constexpr int kChunk = 4; // panels per chunk: 32 source slots, one per producer
 template <int F, int FPW> struct Persist {
     static constexpr int kConsumers = F / FPW;
     static constexpr int kThreads = 32 * (kConsumers + 1);
-    static constexpr int kParts = FPW / 16;     // m16 tiles per consumer warp
-    static constexpr int kLaneBytes = FPW / 8;  // packed bytes of one source per lane (4 or 8)
-    static constexpr int kStages = 6;
-    static constexpr int kALead = 8, kARing = kALead + 1;
-    static constexpr int kVLead = 4, kVRing = kVLead + 1;
-    static_assert(kStages >= kVLead + 2, "a VX step must never wait for the chunk being built");
-    static constexpr int kVCap = 256;           // floats per V slot; larger chunks read values directly
-    static constexpr int kRowStride = F + 32;   // bytes per staged row, 32-byte skew
-    static constexpr int kXBytes = 32 * kRowStride;
+    static constexpr int kParts = FPW / 16;    // m16 tiles per consumer warp
+    static constexpr int kLaneBytes = FPW / 8; // packed bytes of one source per lane (4 or 8)
+    // Consumer X ring (per consumer warp): kPrefetch chunks in flight plus the one computed.
+    static constexpr int kPrefetch = (F == 128) ? 6 : 4;
+    static constexpr int kXDepth = kPrefetch + 1;
+    static constexpr int kXRowStride = FPW == 32 ? 32 : 96; // bytes; conflict-free row loads
+    static constexpr int kXSlotBytes = 32 * kXRowStride;
+    // Producer stages (fragments, scales, masks of one chunk).
+    static constexpr int kStages = 4;
     static constexpr int kScaleBytes = 32 * 4;
     static constexpr int kFragBytes = kChunk * 4 * 32 * 8;
     static constexpr int kMaskBytes = 16;
-    static constexpr int kStageBytes = kXBytes + kScaleBytes + kFragBytes + kMaskBytes;
+    static constexpr int kStageBytes = kScaleBytes + kFragBytes + kMaskBytes;
+    static constexpr int kALead = kPrefetch + 4, kARing = kALead + 2;
+    static constexpr int kVLead = 4, kVRing = kVLead + 1;
+    static constexpr int kVCap = 256;          // values per V slot; larger chunks read them directly
     static constexpr int kASlotBytes = 128 + 256 + 16 + 16; // ids, metadata, masks, header
-    static constexpr int kVSlotBytes = kVCap * 4;
-    static constexpr int kAOff = kStages * kStageBytes;
+    static constexpr int kVSlotBytes = kVCap * 4 + 128;     // values, scales
+    static constexpr int kXOff = 0;
+    static constexpr int kStageOff = kXOff + kConsumers * kXDepth * kXSlotBytes;
+    static constexpr int kAOff = kStageOff + kStages * kStageBytes;
     static constexpr int kVOff = kAOff + kARing * kASlotBytes;
     static constexpr int kVBaseOff = kVOff + kVRing * kVSlotBytes;
     static constexpr int kFlagOff = kVBaseOff + 32;
     static constexpr int kBarOff = kFlagOff + 16;
-    static constexpr int kBars = 2 * kStages + kARing + kVRing;
+    // xFull[kStages], xEmpty[kStages], aFull[kARing], aUsed[kARing], vFull[kVRing]
+    static constexpr int kBars = 2 * kStages + 2 * kARing + kVRing;
     static constexpr int kBytes = kBarOff + 8 * kBars;
-    static_assert(kStageBytes % 16 == 0 && kASlotBytes % 16 == 0 && kBarOff % 8 == 0, "alignment");
+    static_assert(kPrefetch <= kALead, "consumers prefetch only chunks whose IDs are requested");
+    static_assert(kStageBytes % 16 == 0 && kASlotBytes % 16 == 0 && kVSlotBytes % 16 == 0, "alignment");
     static_assert(kVRing <= 8, "vBase area");
 };
 
@@ -79,7 +88,6 @@ __device__ __forceinline__ void namedBarrier(int id, int threads) {
 struct ChunkWalker {
     uint32_t slot, begin, end, next;
     uint32_t nBegin, nEnd;
-    bool done;
     __device__ __forceinline__ void load(const tcc_sw32_device_view& m, uint32_t s, uint32_t& b, uint32_t& e) const {
         const uint64_t t = uint64_t(blockIdx.x) + uint64_t(s) * gridDim.x;
         if (t < m.taskCount) {
@@ -90,12 +98,9 @@ struct ChunkWalker {
         }
     }
     __device__ __forceinline__ void enter(const tcc_sw32_device_view& m) {
-        // Advance from the prefetched task until a non-empty one; prefetch its successor.
         for (;;) {
-            if (nBegin == 0xFFFFFFFFu) {
-                done = true;
+            if (nBegin == 0xFFFFFFFFu)
                 return;
-            }
             begin = nBegin;
             end = nEnd;
             ++slot;
@@ -107,7 +112,7 @@ struct ChunkWalker {
     }
     __device__ __forceinline__ void start(const tcc_sw32_device_view& m) {
         slot = 0xFFFFFFFFu; // enter() increments to 0
-        done = false;
+        begin = end = next = 0;
         load(m, 0, nBegin, nEnd);
         enter(m);
     }
@@ -117,6 +122,50 @@ struct ChunkWalker {
             enter(m);
     }
 };
+
+// Chunks of this CTA (computed by every warp).
+__device__ __forceinline__ uint32_t ctaChunkCount(const tcc_sw32_device_view& m, int lane) {
+    uint32_t total = 0;
+    for (uint64_t t = blockIdx.x + uint64_t(lane) * gridDim.x; t < m.taskCount; t += 32ull * gridDim.x)
+        total += (m.tasks[t].end - m.tasks[t].begin + kChunk - 1) / kChunk;
+    return __reduce_add_sync(0xFFFFFFFFu, total);
+}
+
+// Consumer X step: gather warp c's FPW-byte slice of the 32 source rows of chunk s into its X
+// ring (16-byte cp.async pieces, padding slots zero-filled) as one cp.async group, then tell the
+// producer that the chunk's A slot has been read. Returns false when the A wait ran out.
+template <int F, int FPW>
+__device__ __forceinline__ bool gatherRows(unsigned char* smem, unsigned char* xring, uint32_t barA, uint32_t barU,
+                                           const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
+                                           uint32_t s, int lane, int c, uint64_t policy, bool ok) {
+    using L = Persist<F, FPW>;
+    if (ok && s < total) {
+        const uint32_t aslot = s % L::kARing;
+        if (!boundedWait(barA + 8 * aslot, (s / L::kARing) & 1)) {
+            ok = false;
+        } else {
+            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const uint32_t np = reinterpret_cast<const uint32_t*>(a + 400)[1];
+            unsigned char* dst = xring + (s % L::kXDepth) * L::kXSlotBytes;
+            constexpr int kPieces = FPW / 16, kRowsPerPass = 32 / kPieces;
+#pragma unroll
+            for (int pass = 0; pass < kPieces; ++pass) {
+                const int row = pass * kRowsPerPass + lane / kPieces, piece = lane % kPieces;
+                const uint32_t id = uint32_t(row >> 3) < np ? reinterpret_cast<const uint32_t*>(a)[row] : 0xFFFFFFFFu;
+                const bool valid = id < cols;
+                dev::cpAsync16Hint(dev::smemAddr(dst + row * L::kXRowStride + 16 * piece),
+                                   valid ? static_cast<const void*>(packedX + uint64_t(id) * F + c * FPW + 16 * piece)
+                                         : static_cast<const void*>(packedX),
+                                   valid ? 16u : 0u, policy);
+            }
+            __syncwarp();
+            if (lane == 0)
+                dev::mbarArrive(barU + 8 * aslot);
+        }
+    }
+    dev::cpAsyncCommit();
+    return ok;
+}
 
 template <int F, int FPW>
 __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
@@ -128,42 +177,48 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t base = dev::smemAddr(smem);
-    const uint32_t barX = base + L::kBarOff;   // stage full   [kStages]
-    const uint32_t barE = barX + 8 * L::kStages; // stage empty  [kStages]
-    const uint32_t barA = barE + 8 * L::kStages; // A slot landed [kARing]
-    const uint32_t barV = barA + 8 * L::kARing;  // V slot landed [kVRing]
+    const uint32_t barX = base + L::kBarOff;          // stage full    [kStages]
+    const uint32_t barE = barX + 8 * L::kStages;      // stage empty   [kStages]
+    const uint32_t barA = barE + 8 * L::kStages;      // A slot landed [kARing]
+    const uint32_t barU = barA + 8 * L::kARing;       // A slot read by all consumers [kARing]
+    const uint32_t barV = barU + 8 * L::kARing;       // V slot landed [kVRing]
     volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(smem + L::kFlagOff);
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::kStages; ++s) {
-            dev::mbarInit(barX + 8 * s, 64); // 32 cp.async arrivals (scales) + 32 producer arrivals
+            dev::mbarInit(barX + 8 * s, 32);
             dev::mbarInit(barE + 8 * s, L::kConsumers);
         }
-        for (int s = 0; s < L::kARing; ++s)
+        for (int s = 0; s < L::kARing; ++s) {
             dev::mbarInit(barA + 8 * s, 32);
+            dev::mbarInit(barU + 8 * s, L::kConsumers);
+        }
         for (int s = 0; s < L::kVRing; ++s)
             dev::mbarInit(barV + 8 * s, 32);
         flags[0] = flags[1] = flags[2] = flags[3] = 0;
         dev::fenceBarrierInit();
     }
     __syncthreads();
+    const uint32_t total = ctaChunkCount(matrix, lane);
 
     if (warp == L::kConsumers) {
         // ==================================== producer ====================================
+        const uint64_t polStream = dev::policyEvictFirst();
+        const uint64_t polKeep = dev::policyEvictLast();
         uint32_t* vBase = reinterpret_cast<uint32_t*>(smem + L::kVBaseOff);
         const int pp = lane >> 3, k = lane & 7;
-        // Total chunks of this CTA.
-        uint32_t total = 0;
-        for (uint64_t t = blockIdx.x + uint64_t(lane) * gridDim.x; t < matrix.taskCount; t += 32ull * gridDim.x)
-            total += (matrix.tasks[t].end - matrix.tasks[t].begin + kChunk - 1) / kChunk;
-        total = __reduce_add_sync(0xFFFFFFFFu, total);
         ChunkWalker walk;
         walk.start(matrix);
         uint32_t seqA = 0, seqV = 0;
         bool ok = true;
         for (uint32_t seqF = 0; seqF < total && ok; ++seqF) {
-            // ---- A steps ----
+            // ---- A steps: IDs, metadata, masks of chunks up to seqF + kALead ----
             for (; seqA < total && seqA <= seqF + L::kALead; ++seqA) {
                 const uint32_t slot = seqA % L::kARing;
+                if (seqA >= uint32_t(L::kARing) &&
+                    !boundedWait(barU + 8 * slot, ((seqA / L::kARing) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
                 unsigned char* a = smem + L::kAOff + slot * L::kASlotBytes;
                 const uint32_t p0 = walk.next;
                 const uint32_t np = min(uint32_t(kChunk), walk.end - p0);
@@ -173,38 +228,35 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                 }
                 if (uint32_t(pp) < np) {
                     const uint64_t s = uint64_t(p0 + pp) * 8 + k;
-                    dev::cpAsync4(dev::smemAddr(a + 4 * lane), matrix.sourceIds + s, 4);
-                    dev::cpAsync8(dev::smemAddr(a + 128 + 8 * lane), matrix.sourceMetadata + s);
+                    dev::cpAsync4Hint(dev::smemAddr(a + 4 * lane), matrix.sourceIds + s, 4, polStream);
+                    dev::cpAsync8Hint(dev::smemAddr(a + 128 + 8 * lane), matrix.sourceMetadata + s, polStream);
                 }
                 if (uint32_t(lane) < np)
-                    dev::cpAsync4(dev::smemAddr(a + 384 + 4 * lane), matrix.rowGroupMasks + p0 + lane, 4);
+                    dev::cpAsync4Hint(dev::smemAddr(a + 384 + 4 * lane), matrix.rowGroupMasks + p0 + lane, 4,
+                                      polStream);
                 dev::cpAsyncArriveNoinc(barA + 8 * slot);
                 walk.advance(matrix);
             }
+            if (!ok)
+                break;
             __syncwarp();
-            // ---- VX steps: X rows, scales and values of chunks up to seqF + kVLead ----
+            // ---- V steps: value ranges and scales of chunks up to seqF + kVLead ----
             for (; seqV < seqA && seqV <= seqF + L::kVLead; ++seqV) {
-                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing, stage = seqV % L::kStages;
-                if (!boundedWait(barA + 8 * aslot, (seqV / L::kARing) & 1) ||
-                    (seqV >= L::kStages && !boundedWait(barE + 8 * stage, ((seqV / L::kStages) - 1) & 1))) {
+                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing;
+                if (!boundedWait(barA + 8 * aslot, (seqV / L::kARing) & 1)) {
                     ok = false;
                     break;
                 }
                 const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+                unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
                 const uint32_t np = reinterpret_cast<const uint32_t*>(a + 400)[1];
                 const bool inRange = uint32_t(pp) < np;
                 const uint32_t id = inRange ? *reinterpret_cast<const uint32_t*>(a + 4 * lane) : 0xFFFFFFFFu;
                 const uint64_t meta = inRange ? *reinterpret_cast<const uint64_t*>(a + 128 + 8 * lane) : 0ull;
                 const bool valid = id < cols;
-                unsigned char* st = smem + stage * L::kStageBytes;
-                const uint32_t bar = barX + 8 * stage;
-                dev::mbarExpectTx(bar, valid ? uint32_t(F) : 0u);
-                if (valid)
-                    dev::bulkCopyG2S(dev::smemAddr(st + lane * L::kRowStride), packedX + uint64_t(id) * F, F, bar);
-                dev::cpAsync4(dev::smemAddr(st + L::kXBytes + 4 * (pp * 8 + 2 * (k & 3) + (k >> 2))),
-                              valid ? static_cast<const void*>(scales + id) : static_cast<const void*>(scales),
-                              valid ? 4u : 0u);
-                dev::cpAsyncArriveNoinc(bar);
+                dev::cpAsync4Hint(dev::smemAddr(v + 4 * L::kVCap + 4 * lane),
+                                  valid ? static_cast<const void*>(scales + id) : static_cast<const void*>(scales),
+                                  valid ? 4u : 0u, polKeep);
                 // Values of a chunk are contiguous in slot order.
                 const uint32_t mask = static_cast<uint32_t>(meta);
                 const uint32_t first = static_cast<uint32_t>(meta >> 32);
@@ -213,28 +265,32 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                 const uint32_t count = hi > lo ? hi - lo : 0u;
                 if (lane == 0)
                     vBase[vslot] = count <= uint32_t(L::kVCap) ? lo : 0xFFFFFFFFu;
-                if (count <= uint32_t(L::kVCap)) {
-                    unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
+                if (count <= uint32_t(L::kVCap))
                     for (uint32_t i = lane; i < count; i += 32)
-                        dev::cpAsync4(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4);
-                }
+                        dev::cpAsync4Hint(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4, polStream);
                 dev::cpAsyncArriveNoinc(barV + 8 * vslot);
             }
             if (!ok)
                 break;
-            // ---- F step: B fragments and masks of chunk seqF; publish the stage ----
+            // ---- F step: fragments, scales and masks of chunk seqF; publish the stage ----
             const uint32_t aslot = seqF % L::kARing, vslot = seqF % L::kVRing, stage = seqF % L::kStages;
-            if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1)) {
+            if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1) ||
+                (seqF >= uint32_t(L::kStages) && !boundedWait(barE + 8 * stage, ((seqF / L::kStages) - 1) & 1))) {
                 ok = false;
                 break;
             }
             const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
             const uint32_t np = reinterpret_cast<const uint32_t*>(a + 400)[1];
-            unsigned char* st = smem + stage * L::kStageBytes;
-            uint32_t* stMask = reinterpret_cast<uint32_t*>(st + L::kXBytes + L::kScaleBytes + L::kFragBytes);
+            unsigned char* st = smem + L::kStageOff + stage * L::kStageBytes;
+            float* stScale = reinterpret_cast<float*>(st);
+            float* frag = reinterpret_cast<float*>(st + L::kScaleBytes);
+            uint32_t* stMask = reinterpret_cast<uint32_t*>(st + L::kScaleBytes + L::kFragBytes);
+            // scale of slot k of panel pp -> [pp][2*(k&3) + (k>>2)]: consumer lane t reads (s_t, s_t+4)
+            stScale[pp * 8 + 2 * (k & 3) + (k >> 2)] = reinterpret_cast<const float*>(v + 4 * L::kVCap)[lane];
             if (lane < kChunk)
-                stMask[lane] = uint32_t(lane) < np ? (*reinterpret_cast<const uint32_t*>(a + 384 + 4 * lane) & 15u) : 0u;
-            float* frag = reinterpret_cast<float*>(st + L::kXBytes + L::kScaleBytes);
+                stMask[lane] =
+                    uint32_t(lane) < np ? (*reinterpret_cast<const uint32_t*>(a + 384 + 4 * lane) & 15u) : 0u;
             {
                 uint4* z = reinterpret_cast<uint4*>(frag);
 #pragma unroll
@@ -246,7 +302,7 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
             uint32_t mask = static_cast<uint32_t>(meta);
             const uint32_t first = static_cast<uint32_t>(meta >> 32);
             const uint32_t vb = vBase[vslot];
-            const float* vsm = reinterpret_cast<const float*>(smem + L::kVOff + vslot * L::kVSlotBytes);
+            const float* vsm = reinterpret_cast<const float*>(v);
             uint32_t j = 0;
             while (mask) {
                 const int bit = __ffs(mask) - 1;
@@ -266,8 +322,12 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
         // ==================================== consumers ===================================
         const int g = lane >> 2, t = lane & 3;
         const int c = warp;
-        uint32_t seq = 0;
+        const uint64_t polKeep = dev::policyEvictLast();
+        unsigned char* xring = smem + L::kXOff + c * L::kXDepth * L::kXSlotBytes;
         bool ok = true;
+        for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
+            ok = gatherRows<F, FPW>(smem, xring, barA, barU, packedX, cols, total, s, lane, c, polKeep, ok);
+        uint32_t seq = 0;
         // After a wait runs out (ok == false) the consumers keep walking their tasks without
         // waiting or computing, so every named barrier below is still reached by all of them.
         tcc_sw32_task nextTask{};
@@ -288,23 +348,27 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                     for (int i = 0; i < 4; ++i)
                         acc[r][jj][i] = 0.0f;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                ok = gatherRows<F, FPW>(smem, xring, barA, barU, packedX, cols, total, seq + L::kPrefetch, lane, c,
+                                        polKeep, ok);
+                dev::cpAsyncWaitGroup<L::kPrefetch>();
+                __syncwarp();
                 const uint32_t stage = seq % L::kStages;
                 if (ok && !boundedWait(barX + 8 * stage, (seq / L::kStages) & 1))
                     ok = false;
                 if (!ok)
                     continue;
-                const unsigned char* st = smem + stage * L::kStageBytes;
-                const float2* sc2 = reinterpret_cast<const float2*>(st + L::kXBytes);
-                const float2* frag2 = reinterpret_cast<const float2*>(st + L::kXBytes + L::kScaleBytes);
-                const uint32_t* stMask =
-                    reinterpret_cast<const uint32_t*>(st + L::kXBytes + L::kScaleBytes + L::kFragBytes);
+                const unsigned char* st = smem + L::kStageOff + stage * L::kStageBytes;
+                const float2* sc2 = reinterpret_cast<const float2*>(st);
+                const float2* frag2 = reinterpret_cast<const float2*>(st + L::kScaleBytes);
+                const uint32_t* stMask = reinterpret_cast<const uint32_t*>(st + L::kScaleBytes + L::kFragBytes);
+                const unsigned char* xs = xring + (seq % L::kXDepth) * L::kXSlotBytes;
                 const uint32_t inChunk = min(uint32_t(kChunk), panelCount - ch * kChunk);
                 for (uint32_t pp = 0; pp < inChunk; ++pp) {
                     const uint32_t m = stMask[pp];
                     const float2 s = sc2[pp * 4 + t];
                     const unsigned long long sa = dev::pack2(s.x, s.x), sb = dev::pack2(s.y, s.y);
-                    const unsigned char* rowA = st + (pp * 8 + t) * L::kRowStride + c * FPW + L::kLaneBytes * g;
-                    const unsigned char* rowB = rowA + 4 * L::kRowStride;
+                    const unsigned char* rowA = xs + (pp * 8 + t) * L::kXRowStride + L::kLaneBytes * g;
+                    const unsigned char* rowB = rowA + 4 * L::kXRowStride;
                     uint32_t da[L::kParts * 2], db[L::kParts * 2]; // dequantized sources t and t+4
                     if constexpr (L::kLaneBytes == 8) {
                         const uint2 wa = *reinterpret_cast<const uint2*>(rowA);
@@ -319,12 +383,10 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                         db[0] = t0[0]; db[1] = t0[1]; db[2] = t0[2]; db[3] = t0[3];
                         db[4] = t1[0]; db[5] = t1[1]; db[6] = t1[2]; db[7] = t1[3];
                     } else {
-                        const uint32_t wa = *reinterpret_cast<const uint32_t*>(rowA);
-                        const uint32_t wb = *reinterpret_cast<const uint32_t*>(rowB);
                         uint32_t t0[4];
-                        dev::dequant4(wa, sa, t0);
+                        dev::dequant4(*reinterpret_cast<const uint32_t*>(rowA), sa, t0);
                         da[0] = t0[0]; da[1] = t0[1]; da[2] = t0[2]; da[3] = t0[3];
-                        dev::dequant4(wb, sb, t0);
+                        dev::dequant4(*reinterpret_cast<const uint32_t*>(rowB), sb, t0);
                         db[0] = t0[0]; db[1] = t0[1]; db[2] = t0[2]; db[3] = t0[3];
                     }
 #pragma unroll
@@ -334,7 +396,8 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                             const uint32_t f0 = __float_as_uint(bf.x), f1 = __float_as_uint(bf.y);
 #pragma unroll
                             for (int jj = 0; jj < L::kParts; ++jj)
-                                dev::mmaTf32(acc[rw][jj], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], f0, f1);
+                                dev::mmaTf32(acc[rw][jj], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], f0,
+                                             f1);
                         }
                     }
                 }
@@ -391,22 +454,23 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                     const tcc_sw32_reduce_range red = matrix.reductions[task.reduceFirst + rw];
                     const uint32_t validRows = min(8u, rows - row0);
                     for (uint32_t e = threadIdx.x; e < validRows * kVec; e += 32 * L::kConsumers) {
-                        const uint32_t r = e / kVec, v = e % kVec;
+                        const uint32_t r = e / kVec, vv = e % kVec;
                         float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
                         for (uint32_t item = red.begin; item < red.end; ++item) {
                             const uint64_t blk = matrix.partialIds[item];
-                            const float4 p = __ldcg(reinterpret_cast<const float4*>(partials + (blk * 8 + r) * F) + v);
+                            const float4 p = __ldcg(reinterpret_cast<const float4*>(partials + (blk * 8 + r) * F) + vv);
                             sum.x += p.x;
                             sum.y += p.y;
                             sum.z += p.z;
                             sum.w += p.w;
                         }
-                        __stcs(reinterpret_cast<float4*>(output + uint64_t(row0 + r) * F) + v, sum);
+                        __stcs(reinterpret_cast<float4*>(output + uint64_t(row0 + r) * F) + vv, sum);
                     }
                 }
             }
             namedBarrier(1, 32 * L::kConsumers); // flags[0] is reused by the next split task
         }
+        dev::cpAsyncWaitAll();
         if (!ok)
             flags[1] = 1;
     }
