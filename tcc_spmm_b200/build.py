@@ -45,7 +45,7 @@ def build_library(force: bool = False, verbose_ptxas: bool = False) -> Path:
     LIBDIR.mkdir(exist_ok=True)
     obj_dir = BUILD / "obj"
     obj_dir.mkdir(parents=True, exist_ok=True)
-    headers = sorted(CSRC.glob("*.h*")) + sorted(INCLUDE.rglob("*.h*"))
+    headers = sorted(p for d in (CSRC, INCLUDE) for ext in ("*.h", "*.hpp", "*.cuh") for p in d.rglob(ext))
     objs = []
     for name in LIB_SOURCES:
         src = CSRC / name

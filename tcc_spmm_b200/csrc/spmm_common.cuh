@@ -14,16 +14,24 @@ namespace {
 constexpr uint32_t kNoPartial = 0xFFFFFFFFu;
 constexpr uint64_t kWaitLimitNs = 2000000000ull; // about two seconds per wait
 
+// Wait for the given phase of an mbarrier. The warp is suspended by the hardware between
+// attempts (no busy spin); the timer is read once every 64 attempts and the wait gives up
+// after kWaitLimitNs, recording bit 0 of the status word.
 __device__ __forceinline__ bool boundedWait(uint32_t bar, uint32_t parity) {
     if (dev::mbarTryWait(bar, parity))
         return true;
-    const uint64_t start = dev::globalTimerNs();
-    for (;;) {
-        if (dev::mbarTryWait(bar, parity))
+    uint64_t start = 0;
+    for (uint32_t attempt = 1;; ++attempt) {
+        if (dev::mbarTryWaitSuspend(bar, parity, 2000u))
             return true;
-        if (dev::globalTimerNs() - start > kWaitLimitNs) {
-            atomicOr(&gDeviceStatus, 1u);
-            return false;
+        if ((attempt & 63u) == 0) {
+            const uint64_t now = dev::globalTimerNs();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                atomicOr(&gDeviceStatus, 1u);
+                return false;
+            }
         }
     }
 }

@@ -23,10 +23,33 @@ __device__ __forceinline__ uint32_t tf32Exact(float v) {
 // D(16x8) += A(16x8, row-major) * B(8x8, column-major), TF32 inputs, FP32 accumulate.
 __device__ __forceinline__ void mmaTf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
-                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory loads by 32-bit shared address (always LDS, cheap address arithmetic).
+__device__ __forceinline__ uint32_t ldsU32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 ldsV2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ldsV4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ldsU64(uint32_t addr) {
+    unsigned long long v;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    return v;
 }
 
 // ---- packed FP32 pairs (sm_100a add/mul .f32x2) -----------------------------------------
@@ -88,6 +111,18 @@ __device__ __forceinline__ bool mbarTryWait(uint32_t bar, uint32_t parity) {
                  "selp.u32 %0, 1, 0, p;\n\t}"
                  : "=r"(done)
                  : "r"(bar), "r"(parity)
+                 : "memory");
+    return done != 0;
+}
+// try_wait that lets the hardware suspend the warp for up to `hintNs` nanoseconds (it resumes
+// as soon as the phase completes), so waiting warps do not take issue slots.
+__device__ __forceinline__ bool mbarTryWaitSuspend(uint32_t bar, uint32_t parity, uint32_t hintNs) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done)
+                 : "r"(bar), "r"(parity), "r"(hintNs)
                  : "memory");
     return done != 0;
 }

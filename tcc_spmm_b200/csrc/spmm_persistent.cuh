@@ -41,18 +41,24 @@ template <int F, int FPW> struct Persist {
     static constexpr int kParts = FPW / 16;    // m16 tiles per consumer warp
     static constexpr int kLaneBytes = FPW / 8; // packed bytes of one source per lane (4 or 8)
     // Consumer X ring (per consumer warp): kPrefetch chunks in flight plus the one computed.
-    static constexpr int kPrefetch = (F == 128) ? 6 : 4;
-    static constexpr int kXDepth = kPrefetch + 1;
+    // Ring sizes are powers of two (slot = sequence & (size - 1)).
+    static constexpr int kXDepth = 4;
+    static constexpr int kPrefetch = kXDepth - 1;
     static constexpr int kXRowStride = FPW == 32 ? 32 : 96; // bytes; conflict-free row loads
     static constexpr int kXSlotBytes = 32 * kXRowStride;
-    // Producer stages (fragments, scales, masks of one chunk).
+    // Producer stages (fragments, scales, masks of one chunk). Scales are stored per panel and
+    // fragment column t as (s_t, s_t, s_t+4, s_t+4), ready for the packed f32x2 multiply.
     static constexpr int kStages = 4;
-    static constexpr int kScaleBytes = 32 * 4;
+    static constexpr int kScaleBytes = kChunk * 4 * 16;
     static constexpr int kFragBytes = kChunk * 4 * 32 * 8;
     static constexpr int kMaskBytes = 16;
     static constexpr int kStageBytes = kScaleBytes + kFragBytes + kMaskBytes;
-    static constexpr int kALead = kPrefetch + 4, kARing = kALead + 2;
-    static constexpr int kVLead = 4, kVRing = kVLead + 1;
+    static constexpr int kALead = 6, kARing = 8;
+    static constexpr int kVLead = 3, kVRing = 4;
+    static_assert(kARing >= kALead + 2 && kVRing >= kVLead + 1, "ring sizes");
+    static_assert((kARing & (kARing - 1)) == 0 && (kVRing & (kVRing - 1)) == 0 && (kStages & (kStages - 1)) == 0 &&
+                      (kXDepth & (kXDepth - 1)) == 0,
+                  "power-of-two rings");
     static constexpr int kVCap = 256;          // values per V slot; larger chunks read them directly
     static constexpr int kASlotBytes = 128 + 256 + 16 + 16; // ids, metadata, masks, header
     static constexpr int kVSlotBytes = kVCap * 4 + 128;     // values, scales
@@ -286,8 +292,12 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
             float* stScale = reinterpret_cast<float*>(st);
             float* frag = reinterpret_cast<float*>(st + L::kScaleBytes);
             uint32_t* stMask = reinterpret_cast<uint32_t*>(st + L::kScaleBytes + L::kFragBytes);
-            // scale of slot k of panel pp -> [pp][2*(k&3) + (k>>2)]: consumer lane t reads (s_t, s_t+4)
-            stScale[pp * 8 + 2 * (k & 3) + (k >> 2)] = reinterpret_cast<const float*>(v + 4 * L::kVCap)[lane];
+            // scale of slot k of panel pp -> both halves of pair (k>>2) of entry [pp][k&3]:
+            // consumer lane t reads (s_t, s_t, s_t+4, s_t+4) with one 16-byte load
+            {
+                const float sk = reinterpret_cast<const float*>(v + 4 * L::kVCap)[lane];
+                *reinterpret_cast<float2*>(stScale + (pp * 4 + (k & 3)) * 4 + 2 * (k >> 2)) = make_float2(sk, sk);
+            }
             if (lane < kChunk)
                 stMask[lane] =
                     uint32_t(lane) < np ? (*reinterpret_cast<const uint32_t*>(a + 384 + 4 * lane) & 15u) : 0u;
@@ -324,6 +334,8 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
         const int c = warp;
         const uint64_t polKeep = dev::policyEvictLast();
         unsigned char* xring = smem + L::kXOff + c * L::kXDepth * L::kXSlotBytes;
+        const uint32_t xringA = dev::smemAddr(xring);
+        const uint32_t laneX = t * L::kXRowStride + L::kLaneBytes * g; // this lane's bytes of row t
         bool ok = true;
         for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
             ok = gatherRows<F, FPW>(smem, xring, barA, barU, packedX, cols, total, s, lane, c, polKeep, ok);
@@ -357,22 +369,23 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                     ok = false;
                 if (!ok)
                     continue;
-                const unsigned char* st = smem + L::kStageOff + stage * L::kStageBytes;
-                const float2* sc2 = reinterpret_cast<const float2*>(st);
-                const float2* frag2 = reinterpret_cast<const float2*>(st + L::kScaleBytes);
-                const uint32_t* stMask = reinterpret_cast<const uint32_t*>(st + L::kScaleBytes + L::kFragBytes);
-                const unsigned char* xs = xring + (seq % L::kXDepth) * L::kXSlotBytes;
+                const uint32_t stA = base + L::kStageOff + stage * L::kStageBytes;
+                const uint32_t xsA = xringA + (seq & (L::kXDepth - 1)) * L::kXSlotBytes + laneX;
                 const uint32_t inChunk = min(uint32_t(kChunk), panelCount - ch * kChunk);
-                for (uint32_t pp = 0; pp < inChunk; ++pp) {
-                    const uint32_t m = stMask[pp];
-                    const float2 s = sc2[pp * 4 + t];
-                    const unsigned long long sa = dev::pack2(s.x, s.x), sb = dev::pack2(s.y, s.y);
-                    const unsigned char* rowA = xs + (pp * 8 + t) * L::kXRowStride + L::kLaneBytes * g;
-                    const unsigned char* rowB = rowA + 4 * L::kXRowStride;
+#pragma unroll
+                for (uint32_t pp = 0; pp < uint32_t(kChunk); ++pp) {
+                    if (pp >= inChunk)
+                        break;
+                    const uint32_t m = dev::ldsU32(stA + L::kScaleBytes + L::kFragBytes + 4 * pp);
+                    const uint4 s = dev::ldsV4(stA + 16 * (pp * 4 + t)); // (s_t, s_t, s_t+4, s_t+4)
+                    const unsigned long long sa = (static_cast<unsigned long long>(s.y) << 32) | s.x;
+                    const unsigned long long sb = (static_cast<unsigned long long>(s.w) << 32) | s.z;
+                    const uint32_t rowA = xsA + pp * 8 * L::kXRowStride;
+                    const uint32_t rowB = rowA + 4 * L::kXRowStride;
                     uint32_t da[L::kParts * 2], db[L::kParts * 2]; // dequantized sources t and t+4
                     if constexpr (L::kLaneBytes == 8) {
-                        const uint2 wa = *reinterpret_cast<const uint2*>(rowA);
-                        const uint2 wb = *reinterpret_cast<const uint2*>(rowB);
+                        const uint2 wa = dev::ldsV2(rowA);
+                        const uint2 wb = dev::ldsV2(rowB);
                         uint32_t t0[4], t1[4];
                         dev::dequant4(wa.x, sa, t0);
                         dev::dequant4(wa.y, sa, t1);
@@ -384,20 +397,20 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                         db[4] = t1[0]; db[5] = t1[1]; db[6] = t1[2]; db[7] = t1[3];
                     } else {
                         uint32_t t0[4];
-                        dev::dequant4(*reinterpret_cast<const uint32_t*>(rowA), sa, t0);
+                        dev::dequant4(dev::ldsU32(rowA), sa, t0);
                         da[0] = t0[0]; da[1] = t0[1]; da[2] = t0[2]; da[3] = t0[3];
-                        dev::dequant4(*reinterpret_cast<const uint32_t*>(rowB), sb, t0);
+                        dev::dequant4(dev::ldsU32(rowB), sb, t0);
                         db[0] = t0[0]; db[1] = t0[1]; db[2] = t0[2]; db[3] = t0[3];
                     }
+                    const uint32_t fragA = stA + L::kScaleBytes + 8 * (pp * 4 * 32 + lane);
 #pragma unroll
                     for (int rw = 0; rw < 4; ++rw) {
                         if (m & (1u << rw)) {
-                            const float2 bf = frag2[(pp * 4 + rw) * 32 + lane];
-                            const uint32_t f0 = __float_as_uint(bf.x), f1 = __float_as_uint(bf.y);
+                            const uint2 bf = dev::ldsV2(fragA + 8 * 32 * rw);
 #pragma unroll
                             for (int jj = 0; jj < L::kParts; ++jj)
-                                dev::mmaTf32(acc[rw][jj], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], f0,
-                                             f1);
+                                dev::mmaTf32(acc[rw][jj], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], bf.x,
+                                             bf.y);
                         }
                     }
                 }

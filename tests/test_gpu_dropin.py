@@ -27,7 +27,7 @@ def _write_mtx(path: Path, rows: int, seed: int) -> None:
     lines = [f"%%MatrixMarket matrix coordinate real general", f"{rows} {rows} 0"]
     entries = []
     for r in range(rows):
-        deg = int(rng.integers(0, 40)) if r % 97 else 2000  # a few heavy rows -> split windows
+        deg = int(rng.integers(0, 40)) if r % 97 else 4000  # a few heavy rows -> split windows
         cols = rng.integers(0, rows, size=deg)
         vals = rng.uniform(-1, 1, size=deg)
         entries += [f"{r + 1} {c + 1} {v:.6f}" for c, v in zip(cols, vals)]
@@ -52,7 +52,7 @@ def _reference_features(rows: int, features: int) -> np.ndarray:
 @pytest.mark.parametrize("features", [128, 256])
 def test_reference_driver_runs_on_new_library(tmp_path, features):
     mtx = tmp_path / "m.mtx"
-    _write_mtx(mtx, 5000, features)
+    _write_mtx(mtx, 20000, features)
     ms_new, y_new = _run(DROPIN, mtx, features)
     m = T.load_matrix_market(str(mtx))
     fmt = T.convert_csr_to_sw32(m.rows, m.cols, m.csr)
