@@ -51,7 +51,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--variant", default="default",
-                   choices=["default", "generic", "persistent32", "persistent64"],
+                   choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
+                            "persistent32x4", "persistent64x4"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()

@@ -327,7 +327,8 @@ def _np_of(torch_dtype):
     return {torch.int32: np.int32, torch.int64: np.int64, torch.float32: np.float32}[torch_dtype]
 
 
-KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3}
+KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "persistent32x2": 4,
+                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7}
 
 
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,

@@ -34,18 +34,18 @@ void throwIf(cudaError_t s) {
 
 // Grid of the persistent kernel on `device`: SMs x resident CTAs per SM (computed once per
 // device and kernel variant).
-template <int F, int FPW> uint32_t persistentGrid(int device) {
+template <int F, int FPW, int P> uint32_t persistentGrid(int device) {
     static std::mutex mutex;
     static int grid[64] = {};
     std::lock_guard<std::mutex> lock(mutex);
     if (device < 0 || device >= 64)
         throw CudaError("device ordinal out of range");
     if (grid[device] == 0) {
-        using L = Persist<F, FPW>;
-        throwIf(cudaFuncSetAttribute(spmmPersistentKernel<F, FPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        using L = Persist<F, FPW, P>;
+        throwIf(cudaFuncSetAttribute(spmmPersistentKernel<F, FPW, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      L::kBytes));
         int perSm = 0, sms = 0;
-        throwIf(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, spmmPersistentKernel<F, FPW>, L::kThreads,
+        throwIf(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, spmmPersistentKernel<F, FPW, P>, L::kThreads,
                                                               L::kBytes));
         throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
         if (perSm < 1)
@@ -55,18 +55,19 @@ template <int F, int FPW> uint32_t persistentGrid(int device) {
     return static_cast<uint32_t>(grid[device]);
 }
 
-template <int F, int FPW>
+template <int F, int FPW, int P>
 void launchPersistent(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
                       uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
     int device = 0;
     throwIf(cudaGetDevice(&device));
-    const uint32_t grid = std::min<uint32_t>(m.taskCount, persistentGrid<F, FPW>(device));
-    spmmPersistentKernel<F, FPW><<<grid, Persist<F, FPW>::kThreads, Persist<F, FPW>::kBytes, stream>>>(
+    const uint32_t grid = std::min<uint32_t>(m.taskCount, persistentGrid<F, FPW, P>(device));
+    spmmPersistentKernel<F, FPW, P><<<grid, Persist<F, FPW, P>::kThreads, Persist<F, FPW, P>::kBytes, stream>>>(
         m, x, scales, y, rows, cols, partials, counters);
 }
 
 // variant: 0 = default fast path, 1 = generic kernel, 2/3 = persistent kernel with 32/64
-// features per consumer warp.
+// features per consumer warp and one producer warp, 4/5 = the same with two producer warps,
+// 6/7 = with four producer warps.
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
@@ -77,9 +78,17 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,
                                                                              counters);
     } else if (variant == 2) {
-        launchPersistent<F, 32>(m, x, scales, y, rows, cols, partials, counters, stream);
+        launchPersistent<F, 32, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 3) {
+        launchPersistent<F, 64, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 4) {
+        launchPersistent<F, 32, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 5) {
+        launchPersistent<F, 64, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 6) {
+        launchPersistent<F, 32, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else {
-        launchPersistent<F, 64>(m, x, scales, y, rows, cols, partials, counters, stream);
+        launchPersistent<F, 64, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
     throwIf(cudaGetLastError());
 }
@@ -125,7 +134,7 @@ int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
     return tcc::guarded([&] {
-        if (variant < 0 || variant > 3)
+        if (variant < 0 || variant > 7)
             throw std::invalid_argument("unknown SpMM kernel variant");
         tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters,
                            reinterpret_cast<cudaStream_t>(stream), variant);

@@ -35,9 +35,10 @@ namespace {
 
 constexpr int kChunk = 4; // panels per chunk: 32 source slots, one per producer lane
 
-template <int F, int FPW> struct Persist {
+template <int F, int FPW, int P> struct Persist {
     static constexpr int kConsumers = F / FPW;
-    static constexpr int kThreads = 32 * (kConsumers + 1);
+    static constexpr int kProducers = P;
+    static constexpr int kThreads = 32 * (kConsumers + kProducers);
     static constexpr int kParts = FPW / 16;    // m16 tiles per consumer warp
     static constexpr int kLaneBytes = FPW / 8; // packed bytes of one source per lane (4 or 8)
     // Consumer X ring (per consumer warp): kPrefetch chunks in flight plus the one computed.
@@ -56,6 +57,7 @@ template <int F, int FPW> struct Persist {
     static constexpr int kALead = 6, kARing = 8;
     static constexpr int kVLead = 3, kVRing = 4;
     static_assert(kARing >= kALead + 2 && kVRing >= kVLead + 1, "ring sizes");
+    static_assert(kARing % P == 0 && kVRing % P == 0 && kStages % P == 0, "every ring slot has one producer");
     static_assert((kARing & (kARing - 1)) == 0 && (kVRing & (kVRing - 1)) == 0 && (kStages & (kStages - 1)) == 0 &&
                       (kXDepth & (kXDepth - 1)) == 0,
                   "power-of-two rings");
@@ -140,11 +142,11 @@ __device__ __forceinline__ uint32_t ctaChunkCount(const tcc_sw32_device_view& m,
 // Consumer X step: gather warp c's FPW-byte slice of the 32 source rows of chunk s into its X
 // ring (16-byte cp.async pieces, padding slots zero-filled) as one cp.async group, then tell the
 // producer that the chunk's A slot has been read. Returns false when the A wait ran out.
-template <int F, int FPW>
+template <int F, int FPW, int P>
 __device__ __forceinline__ bool gatherRows(unsigned char* smem, unsigned char* xring, uint32_t barA, uint32_t barU,
                                            const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
                                            uint32_t s, int lane, int c, uint64_t policy, bool ok) {
-    using L = Persist<F, FPW>;
+    using L = Persist<F, FPW, P>;
     if (ok && s < total) {
         const uint32_t aslot = s % L::kARing;
         if (!boundedWait(barA + 8 * aslot, (s / L::kARing) & 1)) {
@@ -173,12 +175,12 @@ __device__ __forceinline__ bool gatherRows(unsigned char* smem, unsigned char* x
     return ok;
 }
 
-template <int F, int FPW>
-__global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
+template <int F, int FPW, int P>
+__global__ void __launch_bounds__(Persist<F, FPW, P>::kThreads)
     spmmPersistentKernel(const tcc_sw32_device_view matrix, const int8_t* __restrict__ packedX,
                          const float* __restrict__ scales, float* __restrict__ output, uint32_t rows,
                          uint32_t cols, float* __restrict__ partials, uint32_t* __restrict__ counters) {
-    using L = Persist<F, FPW>;
+    using L = Persist<F, FPW, P>;
     extern __shared__ __align__(128) unsigned char smem[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -206,19 +208,23 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
     __syncthreads();
     const uint32_t total = ctaChunkCount(matrix, lane);
 
-    if (warp == L::kConsumers) {
-        // ==================================== producer ====================================
+    if (warp >= L::kConsumers) {
+        // ==================================== producers ===================================
+        // Producer pw owns the chunks pw, pw+P, pw+2P, ... and every ring slot they map to.
         const uint64_t polStream = dev::policyEvictFirst();
         const uint64_t polKeep = dev::policyEvictLast();
         uint32_t* vBase = reinterpret_cast<uint32_t*>(smem + L::kVBaseOff);
         const int pp = lane >> 3, k = lane & 7;
+        const uint32_t pw = warp - L::kConsumers;
         ChunkWalker walk;
         walk.start(matrix);
-        uint32_t seqA = 0, seqV = 0;
+        for (uint32_t i = 0; i < pw; ++i)
+            walk.advance(matrix);
+        uint32_t seqA = pw, seqV = pw;
         bool ok = true;
-        for (uint32_t seqF = 0; seqF < total && ok; ++seqF) {
+        for (uint32_t seqF = pw; seqF < total && ok; seqF += P) {
             // ---- A steps: IDs, metadata, masks of chunks up to seqF + kALead ----
-            for (; seqA < total && seqA <= seqF + L::kALead; ++seqA) {
+            for (; seqA < total && seqA <= seqF + L::kALead; seqA += P) {
                 const uint32_t slot = seqA % L::kARing;
                 if (seqA >= uint32_t(L::kARing) &&
                     !boundedWait(barU + 8 * slot, ((seqA / L::kARing) - 1) & 1)) {
@@ -241,13 +247,15 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                     dev::cpAsync4Hint(dev::smemAddr(a + 384 + 4 * lane), matrix.rowGroupMasks + p0 + lane, 4,
                                       polStream);
                 dev::cpAsyncArriveNoinc(barA + 8 * slot);
-                walk.advance(matrix);
+#pragma unroll
+                for (int i = 0; i < P; ++i)
+                    walk.advance(matrix);
             }
             if (!ok)
                 break;
             __syncwarp();
             // ---- V steps: value ranges and scales of chunks up to seqF + kVLead ----
-            for (; seqV < seqA && seqV <= seqF + L::kVLead; ++seqV) {
+            for (; seqV < seqA && seqV <= seqF + L::kVLead; seqV += P) {
                 const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing;
                 if (!boundedWait(barA + 8 * aslot, (seqV / L::kARing) & 1)) {
                     ok = false;
@@ -338,7 +346,7 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
         const uint32_t laneX = t * L::kXRowStride + L::kLaneBytes * g; // this lane's bytes of row t
         bool ok = true;
         for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
-            ok = gatherRows<F, FPW>(smem, xring, barA, barU, packedX, cols, total, s, lane, c, polKeep, ok);
+            ok = gatherRows<F, FPW, P>(smem, xring, barA, barU, packedX, cols, total, s, lane, c, polKeep, ok);
         uint32_t seq = 0;
         // After a wait runs out (ok == false) the consumers keep walking their tasks without
         // waiting or computing, so every named barrier below is still reached by all of them.
@@ -360,7 +368,7 @@ __global__ void __launch_bounds__(Persist<F, FPW>::kThreads)
                     for (int i = 0; i < 4; ++i)
                         acc[r][jj][i] = 0.0f;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
-                ok = gatherRows<F, FPW>(smem, xring, barA, barU, packedX, cols, total, seq + L::kPrefetch, lane, c,
+                ok = gatherRows<F, FPW, P>(smem, xring, barA, barU, packedX, cols, total, seq + L::kPrefetch, lane, c,
                                         polKeep, ok);
                 dev::cpAsyncWaitGroup<L::kPrefetch>();
                 __syncwarp();
