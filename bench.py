@@ -69,14 +69,17 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic(config: str):
+def profile_traffic(config: str, variant: str):
+    """ncu DRAM bytes of one launch of this config's kernel (profiles/traffic.json), when the
+    capture was taken of the same kernel variant."""
     path = ROOT / "profiles" / "traffic.json"
     if not path.exists():
         return None
     try:
-        return json.loads(path.read_text()).get(config)
+        entry = json.loads(path.read_text()).get(config)
     except Exception:
         return None
+    return entry if entry and entry.get("variant", "default") == variant else None
 
 
 # ----------------------------------------------------------------------------------------
@@ -297,7 +300,7 @@ def run_tcc(args):
     peak, peak_kind = measured_peaks()
     launch_s = (ms_local / args.steps) / 1e3
     achieved = shard["total"] / launch_s / 1e9
-    traffic = profile_traffic(args.config) if world == 1 else None
+    traffic = profile_traffic(args.config, args.variant) if world == 1 else None
 
     # end to end: host packed X + scales -> device, SpMM, this rank's Y rows -> host
     e2e = None
