@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
-                            "persistent32x4", "persistent64x4"],
+                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()
@@ -360,6 +360,7 @@ def run_tcc(args):
                    "tasks": int(fmt.tasks.size), "partial_count": fmt.partial_count,
                    "parallelism": f"task-range shards x{world}, X replicated, Y rows per rank",
                    "l2": "inputs larger than L2 (no flush)", "kernel": args.variant,
+                   "launch": T.spmm_launch_shape(F, args.variant) if args.variant != "generic" else None,
                    "prep": prep},
         "hbm_gbs_alg": round(full["total"] / (ms_step / 1e3) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

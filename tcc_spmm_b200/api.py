@@ -328,7 +328,7 @@ def _np_of(torch_dtype):
 
 
 KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "persistent32x2": 4,
-                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7}
+                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7, "tmem2p1": 8, "tmem2p2": 9, "tmem4p2": 10, "tmem4p4": 11}
 
 
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,
@@ -345,6 +345,15 @@ def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int
         _check(N.lib().tcc_launch_spmm_int8(*args))
     else:
         _check(N.lib().tcc_launch_spmm_int8_variant(*args, v))
+
+
+def spmm_launch_shape(features: int, variant: str = "default") -> dict:
+    """Grid, threads per CTA, dynamic shared memory and calculator occupancy (CTAs per SM) of a
+    fast-path SpMM kernel variant on the current device."""
+    g, t, s, o = C.c_uint32(), C.c_uint32(), C.c_uint32(), C.c_int()
+    _check(N.lib().tcc_spmm_launch_shape(features, KERNEL_VARIANTS[variant], C.byref(g), C.byref(t), C.byref(s),
+                                         C.byref(o)))
+    return {"grid": g.value, "threads": t.value, "smem": s.value, "occupancy": o.value}
 
 
 def quantize_features_int8(x, q, scale, sources: int, features: int, stream=None) -> None:

@@ -18,7 +18,9 @@
 #include "common.hpp"
 #include "spmm_generic.cuh"
 #include "spmm_persistent.cuh"
+#include "spmm_tmem.cuh"
 
+#include <algorithm>
 #include <cuda_runtime.h>
 #include <mutex>
 
@@ -65,15 +67,81 @@ void launchPersistent(const tcc_sw32_device_view& m, const int8_t* x, const floa
         m, x, scales, y, rows, cols, partials, counters);
 }
 
+// Launch shape of the tensor-memory kernel on `device`. At most Tmem::kMaxCtasPerSm CTAs may
+// share an SM's 512 TMEM columns (an allocation beyond them would wait for another CTA to
+// finish), so the dynamic shared memory is padded until one more CTA no longer fits. The
+// occupancy calculator reports one CTA per SM for kernels that allocate tensor memory, so the
+// resident count is derived here from the shared-memory, register and thread limits.
+struct LaunchShape {
+    uint32_t grid = 0, smem = 0;
+    int occupancy = 0; // resident CTAs per SM of this launch shape
+};
+template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
+    static std::mutex mutex;
+    static LaunchShape shape[64];
+    std::lock_guard<std::mutex> lock(mutex);
+    if (device < 0 || device >= 64)
+        throw CudaError("device ordinal out of range");
+    if (shape[device].grid == 0) {
+        using L = Tmem<F, STAGES, P>;
+        int perSmBytes = 0, reserved = 0, optin = 0, sms = 0, regsPerSm = 0, threadsPerSm = 0;
+        throwIf(cudaDeviceGetAttribute(&perSmBytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device));
+        throwIf(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device));
+        throwIf(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+        throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        throwIf(cudaDeviceGetAttribute(&regsPerSm, cudaDevAttrMaxRegistersPerMultiprocessor, device));
+        throwIf(cudaDeviceGetAttribute(&threadsPerSm, cudaDevAttrMaxThreadsPerMultiProcessor, device));
+        const int floor = perSmBytes / (L::kMaxCtasPerSm + 1) - reserved + 1;
+        const int bytes = (std::max(L::kBytes, floor) + 127) / 128 * 128;
+        if (bytes > optin)
+            throw CudaError("tensor-memory SpMM kernel does not fit on this device");
+        throwIf(cudaFuncSetAttribute(spmmTmemKernel<F, STAGES, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     bytes));
+        cudaFuncAttributes attr{};
+        throwIf(cudaFuncGetAttributes(&attr, spmmTmemKernel<F, STAGES, P>));
+        // Registers are allocated per warp in units of 256 and each of the 4 SM sub-partitions
+        // holds a quarter of the register file; the warps of the resident CTAs spread evenly.
+        const int warps = L::kThreads / 32;
+        const int regsPerWarp = (attr.numRegs * 32 + 255) / 256 * 256;
+        const int warpsPerQuarter = regsPerWarp > 0 ? (regsPerSm / 4) / regsPerWarp : 64;
+        int perSm = L::kMaxCtasPerSm;
+        perSm = std::min(perSm, perSmBytes / (bytes + reserved));
+        perSm = std::min(perSm, threadsPerSm / L::kThreads);
+        while (perSm > 0 && (perSm * warps + 3) / 4 > warpsPerQuarter)
+            --perSm;
+        if (perSm < 1)
+            throw CudaError("tensor-memory SpMM kernel does not fit on this device");
+        shape[device].occupancy = perSm;
+        shape[device].smem = static_cast<uint32_t>(bytes);
+        shape[device].grid = static_cast<uint32_t>(perSm * sms);
+    }
+    return shape[device];
+}
+
+template <int F, int STAGES, int P>
+void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
+                uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
+    int device = 0;
+    throwIf(cudaGetDevice(&device));
+    const LaunchShape s = tmemShape<F, STAGES, P>(device);
+    const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
+    spmmTmemKernel<F, STAGES, P><<<grid, Tmem<F, STAGES, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols,
+                                                                                         partials, counters);
+}
+
 // variant: 0 = default fast path, 1 = generic kernel, 2/3 = persistent kernel with 32/64
 // features per consumer warp and one producer warp, 4/5 = the same with two producer warps,
-// 6/7 = with four producer warps.
+// 6/7 = with four producer warps, 8..11 = tensor-memory kernel with (stages, producer warps)
+// (2, 1), (2, 2), (4, 2), (4, 4).
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
     if (variant == 0)
         variant = F == 128 ? 2 : 3;
+    // The tensor-memory kernel moves the IDs and metadata with bulk copies (16-byte aligned).
+    if (variant >= 8 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16)))
+        variant = 1;
     if (variant == 1 || !fast) {
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,
                                                                              counters);
@@ -87,8 +155,16 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
         launchPersistent<F, 64, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else if (variant == 6) {
         launchPersistent<F, 32, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else {
+    } else if (variant == 7) {
         launchPersistent<F, 64, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 8) {
+        launchTmem<F, 2, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 9) {
+        launchTmem<F, 2, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 10) {
+        launchTmem<F, 4, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else {
+        launchTmem<F, 4, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
     throwIf(cudaGetLastError());
 }
@@ -134,10 +210,67 @@ int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
     return tcc::guarded([&] {
-        if (variant < 0 || variant > 7)
+        if (variant < 0 || variant > 11)
             throw std::invalid_argument("unknown SpMM kernel variant");
         tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters,
                            reinterpret_cast<cudaStream_t>(stream), variant);
+    });
+}
+
+// Launch shape of a fast-path kernel variant on the current device (tuning and reports; not
+// part of the public header): grid, threads per CTA, dynamic shared memory and the occupancy
+// calculator's resident CTAs per SM. Variant 1 (generic) has a per-call grid: reported as 0.
+int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32_t* threads, uint32_t* smem,
+                          int* occupancy) {
+    return tcc::guarded([&] {
+        if (grid == nullptr || threads == nullptr || smem == nullptr || occupancy == nullptr)
+            throw std::invalid_argument("null output");
+        if (features != 128 && features != 256)
+            throw std::invalid_argument("feature dimension must be 128 or 256");
+        if (variant < 0 || variant > 11)
+            throw std::invalid_argument("unknown SpMM kernel variant");
+        int device = 0, sms = 1;
+        tcc::throwIf(cudaGetDevice(&device));
+        tcc::throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        if (variant == 0)
+            variant = features == 128 ? 2 : 3;
+        *grid = *threads = *smem = 0;
+        *occupancy = 0;
+        auto persistent = [&](auto layout, uint32_t g) {
+            using L = decltype(layout);
+            *grid = g;
+            *threads = L::kThreads;
+            *smem = L::kBytes;
+            *occupancy = static_cast<int>(g) / std::max(1, sms);
+        };
+        auto tmem = [&](auto layout, tcc::LaunchShape s) {
+            using L = decltype(layout);
+            *grid = s.grid;
+            *threads = L::kThreads;
+            *smem = s.smem;
+            *occupancy = s.occupancy;
+        };
+        if (features == 128) {
+            switch (variant) {
+            case 2: persistent(tcc::Persist<128, 32, 1>{}, tcc::persistentGrid<128, 32, 1>(device)); break;
+            case 3: persistent(tcc::Persist<128, 64, 1>{}, tcc::persistentGrid<128, 64, 1>(device)); break;
+            case 8: tmem(tcc::Tmem<128, 2, 1>{}, tcc::tmemShape<128, 2, 1>(device)); break;
+            case 9: tmem(tcc::Tmem<128, 2, 2>{}, tcc::tmemShape<128, 2, 2>(device)); break;
+            case 10: tmem(tcc::Tmem<128, 4, 2>{}, tcc::tmemShape<128, 4, 2>(device)); break;
+            case 11: tmem(tcc::Tmem<128, 4, 4>{}, tcc::tmemShape<128, 4, 4>(device)); break;
+            default: break;
+            }
+        } else {
+            switch (variant) {
+            case 2: persistent(tcc::Persist<256, 32, 1>{}, tcc::persistentGrid<256, 32, 1>(device)); break;
+            case 3: persistent(tcc::Persist<256, 64, 1>{}, tcc::persistentGrid<256, 64, 1>(device)); break;
+            case 8: tmem(tcc::Tmem<256, 2, 1>{}, tcc::tmemShape<256, 2, 1>(device)); break;
+            case 9: tmem(tcc::Tmem<256, 2, 2>{}, tcc::tmemShape<256, 2, 2>(device)); break;
+            case 10: tmem(tcc::Tmem<256, 4, 2>{}, tcc::tmemShape<256, 4, 2>(device)); break;
+            case 11: tmem(tcc::Tmem<256, 4, 4>{}, tcc::tmemShape<256, 4, 4>(device)); break;
+            default: break;
+            }
+        }
     });
 }
 

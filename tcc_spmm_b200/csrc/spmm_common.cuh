@@ -35,5 +35,24 @@ __device__ __forceinline__ bool boundedWait(uint32_t bar, uint32_t parity) {
         }
     }
 }
+// Bounded wait for waits that are usually long (a warp that waits on another role's
+// progress): between attempts the warp sleeps 32 ns, doubling to 256 ns, instead of retrying
+// at once, so it takes almost no issue slots from the warps doing the work.
+__device__ __forceinline__ bool boundedWaitBackoff(uint32_t bar, uint32_t parity) {
+    if (dev::mbarTryWait(bar, parity))
+        return true;
+    const uint64_t start = dev::globalTimerNs();
+    uint32_t ns = 32;
+    for (;;) {
+        __nanosleep(ns);
+        if (dev::mbarTryWait(bar, parity))
+            return true;
+        ns = ns < 256u ? 2 * ns : 256u;
+        if (dev::globalTimerNs() - start > kWaitLimitNs) {
+            atomicOr(&gDeviceStatus, 1u);
+            return false;
+        }
+    }
+}
 } // namespace
 } // namespace tcc

@@ -187,9 +187,97 @@ __device__ __forceinline__ void bulkCopyG2S(uint32_t dst, const void* src, uint3
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
+// Same with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulkCopyG2SHint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                                uint64_t policy) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+                 : "memory");
+}
+// Arrive on `bar` and add `bytes` to the transaction count its current phase waits for.
+__device__ __forceinline__ void mbarArriveExpectTx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void fenceBarrierInit() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Dequantize byte K (K = 0..3) of two source words at once: the packed f32x2 pair holds
+// source a's and source b's byte, scale2 = (scale_a, scale_b). The words are already flipped
+// to unsigned bytes (word ^ 0x80808080). Same arithmetic as dequant4, biased TF32 results
+// (the tensor core drops the low 13 bits).
+template <int K>
+__device__ __forceinline__ void dequantPair(uint32_t wa, uint32_t wb, unsigned long long scale2, uint32_t& outA,
+                                            uint32_t& outB) {
+    const uint32_t magic = 0x4B000000u;
+    const unsigned long long bias2 = 0xCB000080CB000080ull; // (-8388736.f, -8388736.f)
+    const unsigned long long p = (static_cast<unsigned long long>(__byte_perm(wb, magic, 0x7540 + K)) << 32) |
+                                 __byte_perm(wa, magic, 0x7540 + K);
+    const unsigned long long f = mul2(add2(p, bias2), scale2);
+    outA = lo32(f) + 0x1000u;
+    outB = hi32(f) + 0x1000u;
+}
+
+// ---- tensor memory and the 5th-generation tensor core (tcgen05) ---------------------------
+// Allocate `cols` TMEM columns (power of two >= 32) for this CTA; the whole warp executes it
+// and the TMEM address is written to shared memory at `dst`.
+__device__ __forceinline__ void tmemAlloc(uint32_t dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmemRelinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmemDealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tcFenceBefore() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tcFenceAfter() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tcWaitSt() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tcWaitLd() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (the
+// tensor core reads its shared-memory operand through it).
+__device__ __forceinline__ void fenceProxyAsyncShared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Warp store of 16 TMEM lanes x 32 columns (16x256b shape, 4 repetitions along the columns):
+// thread t writes lanes t/4 (r[4j], r[4j+1]) and t/4 + 8 (r[4j+2], r[4j+3]) at columns
+// 8j + 2(t%4) and 8j + 2(t%4) + 1, j = 0..3.
+__device__ __forceinline__ void tcStore16x256bx4(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], "
+                 "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+                 "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+                 : "memory");
+}
+// Warp load of 32 TMEM lanes x 32 columns (32x32b shape, 32 repetitions): thread t reads
+// lane t, r[j] = column j.
+__device__ __forceinline__ void tcLoad32x32bx32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                   "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                   "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                   "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr)
+                 : "memory");
+}
+// D(tmem, M x N, FP32) (+)= A(tmem, M x K, TF32, K-major) * B(smem descriptor, K x N, TF32),
+// one CTA, issued by a single thread. accumulate == 0 overwrites D.
+__device__ __forceinline__ void mmaTf32Ts(uint32_t dTmem, uint32_t aTmem, unsigned long long bDesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+                 ::"r"(dTmem), "r"(aTmem), "l"(bDesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+                 : "memory");
+}
+// Arrive once on the mbarrier when every tcgen05 operation this thread issued so far is done.
+__device__ __forceinline__ void tcCommit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
 }
 
 // Ticket of the in-kernel merge: atomically increments *counter, wrapping to 0 after

@@ -22,7 +22,7 @@ def _torch():
     return torch
 
 
-@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64"])
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"])
 @pytest.mark.parametrize("features", [128, 256])
 @pytest.mark.parametrize("name", sorted(EDGE_CASES))
 def test_edge_cases_within_tf32_bound(name, features, variant):
@@ -49,7 +49,7 @@ def test_seeded_configs_within_tf32_bound(name, features):
     assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, f"{name}/F{features}")
 
 
-@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64"])
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"])
 def test_single_term_rows_bit_exact(variant):
     """One nonzero per row: Y = tf32_rna(a) * tf32_rna(q*s) exactly, which pins the operand
     rounding (round-half-away on 10 mantissa bits) on the tensor cores."""
