@@ -49,6 +49,7 @@ def parse_args():
     p.add_argument("--config", default="powerlaw128")
     p.add_argument("--impl", default="tcc", choices=["tcc", "reference"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--e2e-slices", type=int, default=8, help="window-aligned task slices per end-to-end step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
@@ -155,6 +156,98 @@ def shard_bytes(fmt, lo: int, hi: int, features: int) -> dict:
     return {"total": int(a_bytes + x_bytes + y_bytes), "a_bytes": int(a_bytes), "x_bytes": int(x_bytes),
             "y_bytes": int(y_bytes), "nnz": nnz, "rows": int(rows), "valid_slots": valid, "panels": p1 - p0,
             "row_begin": 32 * sw0, "row_end": min(fmt.rows, 32 * sw1)}
+
+
+def window_cuts(fmt, lo: int, hi: int, parts: int) -> list:
+    """Boundaries (local to [lo, hi)) of about `parts` task slices, each starting at a window
+    boundary so that no window is split between two slices."""
+    sw = fmt.tasks["sw"][lo:hi]
+    n = hi - lo
+    cuts = [0]
+    for k in range(1, parts):
+        t = max(cuts[-1] + 1, (n * k) // parts)
+        while 0 < t < n and sw[t] == sw[t - 1]:
+            t += 1
+        if t < n:
+            cuts.append(t)
+    cuts.append(n)
+    return sorted(set(cuts))
+
+
+def run_e2e(args, T, fmt, dm, lo, hi, packed, scales, F, device, stream, barrier, world, nnz_total):
+    import torch
+    import torch.distributed as dist
+
+    cuts = window_cuts(fmt, lo, hi, args.e2e_slices)
+    slices = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        sw0, sw1 = int(fmt.tasks["sw"][lo + a]), int(fmt.tasks["sw"][lo + b - 1]) + 1
+        slices.append((dm.view(a, b), 32 * sw0, min(fmt.rows, 32 * sw1)))
+    r0, r1 = slices[0][1], slices[-1][2]
+    packed_h = packed.cpu().pin_memory()
+    scales_h = scales.cpu().pin_memory()
+    y_h = torch.empty((max(0, r1 - r0), F), dtype=torch.float32).pin_memory()
+    inputs = [(packed, scales), (torch.empty_like(packed), torch.empty_like(scales))]
+    ys = [torch.empty((fmt.rows, F), dtype=torch.float32, device=device) for _ in range(2)]
+    ws = dm.workspace()
+    h2d = torch.cuda.Stream(device)
+    d2h = torch.cuda.Stream(device)
+    ev = lambda: torch.cuda.Event()
+    in_ready = [ev(), ev()]
+    in_free = [ev(), ev()]
+    y_free = [ev(), ev()]
+
+    def run(steps: int, start=None, stop=None):
+        if start is not None:
+            start.record(stream)
+            h2d.wait_event(start)
+        for i in range(steps + 1):
+            b = i % 2
+            if i < steps:  # inputs of step i (buffer b is free once step i-2 computed)
+                if i >= 2:
+                    h2d.wait_event(in_free[b])
+                with torch.cuda.stream(h2d):
+                    inputs[b][0].copy_(packed_h, non_blocking=True)
+                    inputs[b][1].copy_(scales_h, non_blocking=True)
+                in_ready[b].record(h2d)
+            if i == 0:
+                continue
+            j = i - 1  # compute step j and copy its rows back
+            bj = j % 2
+            stream.wait_event(in_ready[bj])
+            if j >= 2:
+                stream.wait_event(y_free[bj])
+            for view, ra, rb in slices:
+                T.launch_spmm_int8(view, inputs[bj][0], inputs[bj][1], ys[bj], fmt.rows, fmt.cols, F, ws,
+                                   stream=stream, variant=args.variant)
+                done = ev()
+                done.record(stream)
+                d2h.wait_event(done)
+                if rb > ra:
+                    with torch.cuda.stream(d2h):
+                        y_h[ra - r0:rb - r0].copy_(ys[bj][ra:rb], non_blocking=True)
+            in_free[bj].record(stream)
+            y_free[bj].record(d2h)
+        if stop is not None:
+            stream.wait_stream(d2h)
+            stop.record(stream)
+
+    run(max(3, args.warmup))
+    torch.cuda.synchronize()
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    run(args.steps, start, stop)
+    torch.cuda.synchronize()
+    ms = torch.tensor([start.elapsed_time(stop)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    step_ms = float(ms.item()) / args.steps
+    return {"value": nnz_total * F / (step_ms / 1e3), "unit": "nnz*F/s", "ms_per_step": round(step_ms, 4),
+            "h2d_bytes_per_step": int(packed.numel() + 4 * scales.numel()), "d2h_bytes_per_step": int(4 * (r1 - r0) * F),
+            "slices_per_step": len(slices), "gpu_launches": len(slices) * args.steps,
+            "api": "tcc_launch_spmm_int8 (C ABI) via tcc_spmm_b200: DeviceMatrix.view slices, pinned host buffers, "
+                   "copy streams (inputs and Y double-buffered)"}
 
 
 def build_workload(config: str, threads: int, use_reference_format: bool = False):
@@ -302,37 +395,14 @@ def run_tcc(args):
     achieved = shard["total"] / launch_s / 1e9
     traffic = profile_traffic(args.config, args.variant) if world == 1 else None
 
-    # end to end: host packed X + scales -> device, SpMM, this rank's Y rows -> host
+    # end to end through the public API with host buffers: every step copies packed X +
+    # scales host -> device, runs the SpMM and copies this rank's Y rows device -> host. The
+    # step's task range is launched in window-aligned slices so that the copy of finished Y rows
+    # (copy stream) overlaps the remaining slices, and the next step's inputs are copied into a
+    # second buffer while this step computes (inputs and Y are double-buffered).
     e2e = None
     if not args.no_e2e:
-        packed_h = packed.cpu().pin_memory()
-        scales_h = scales.cpu().pin_memory()
-        r0, r1 = shard.get("row_begin", 0), shard.get("row_end", 0)
-        y_h = torch.empty((max(0, r1 - r0), F), dtype=torch.float32).pin_memory()
-
-        def e2e_step():
-            packed.copy_(packed_h, non_blocking=True)
-            scales.copy_(scales_h, non_blocking=True)
-            launch()
-            if r1 > r0:
-                y_h.copy_(y[r0:r1], non_blocking=True)
-
-        for _ in range(max(3, args.warmup)):
-            e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        start.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        stop.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = torch.tensor([start.elapsed_time(stop)], device=device, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-        e2e_step_ms = float(e2e_ms.item()) / args.steps
-        e2e = {"value": nnz_total * F / (e2e_step_ms / 1e3), "unit": "nnz*F/s",
-               "ms_per_step": round(e2e_step_ms, 4), "h2d_bytes_per_step": int(packed.numel() + 4 * scales.numel()),
-               "d2h_bytes_per_step": int(4 * (r1 - r0) * F), "api": "tcc_launch_spmm_int8 (C ABI) via tcc_spmm_b200"}
+        e2e = run_e2e(args, T, fmt, dm, lo, hi, packed, scales, F, device, stream, barrier, world, nnz_total)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

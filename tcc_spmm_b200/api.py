@@ -306,11 +306,19 @@ class DeviceMatrix:
         self.partials = torch.empty(pf, dtype=torch.float32, device=self.device) if pf else None
         self.counters = torch.zeros(cw, dtype=torch.int32, device=self.device) if cw else None
 
-    def view(self) -> N.Sw32DeviceView:
+    def view(self, first: int = 0, last: Optional[int] = None) -> N.Sw32DeviceView:
+        """Device view over the uploaded tasks [first, last) (all by default). A sub-range that
+        starts and ends at window boundaries writes exactly the Y rows of its windows, so
+        several such views can be launched one after another to overlap the copy of finished
+        rows with the rest (the tasks array is shared; each view points into it)."""
+        last = self.task_count if last is None else last
+        if not 0 <= first <= last <= self.task_count:
+            raise ValueError("task range out of bounds")
         return N.Sw32DeviceView(self.window_offsets.data_ptr(), self.source_ids.data_ptr(),
                                 self.row_group_masks.data_ptr(), self.source_metadata.data_ptr(),
-                                self.values.data_ptr(), self.bucket_offsets.data_ptr(), self.tasks.data_ptr(),
-                                self.reductions.data_ptr(), self.partial_ids.data_ptr(), self.task_count)
+                                self.values.data_ptr(), self.bucket_offsets.data_ptr(),
+                                self.tasks.data_ptr() + TASK_DTYPE.itemsize * first, self.reductions.data_ptr(),
+                                self.partial_ids.data_ptr(), last - first)
 
     def workspace(self) -> SpmmWorkspace:
         return SpmmWorkspace(self.partials, self.counters)

@@ -8,9 +8,12 @@
 // [partialCount][8][F] of split tasks and the last-arriver merge with a wrapping
 // acquire-release ticket that returns every counter to zero.
 //
-// Two kernels:
-//   spmmPersistentKernel (spmm_persistent.cuh): the fast path, used when packedX, Y and the
-//     partials are 16-byte aligned (always true for cudaMalloc'd buffers).
+// Three kernels:
+//   spmmTmemKernel (spmm_tmem.cuh): the fast path (tcgen05 MMAs, accumulators in tensor
+//     memory), used when packedX, Y, the partials, sourceIds and sourceMetadata are 16-byte
+//     aligned (always true for cudaMalloc'd buffers).
+//   spmmPersistentKernel (spmm_persistent.cuh): mma.sync with register accumulators, when
+//     only the IDs or metadata are not 16-byte aligned.
 //   spmmGenericKernel (spmm_generic.cuh): any 2-byte aligned packedX (the reference's own
 //     requirement), operands straight from global memory.
 // Every wait is bounded (about two seconds of %globaltimer); a wait that runs out records a
@@ -26,6 +29,8 @@
 
 namespace tcc {
 namespace {
+
+constexpr int kDefaultVariant = 9; // spmmTmemKernel<F, 2, 2>
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -137,11 +142,13 @@ template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
+    // Default: the tensor-memory kernel with two stages and two producer warps. It moves the
+    // IDs and metadata with bulk copies, which need 16-byte aligned arrays; otherwise the
+    // persistent kernel runs.
     if (variant == 0)
-        variant = F == 128 ? 2 : 3;
-    // The tensor-memory kernel moves the IDs and metadata with bulk copies (16-byte aligned).
+        variant = kDefaultVariant;
     if (variant >= 8 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16)))
-        variant = 1;
+        variant = F == 128 ? 2 : 3;
     if (variant == 1 || !fast) {
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,
                                                                              counters);
@@ -233,7 +240,7 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
         tcc::throwIf(cudaGetDevice(&device));
         tcc::throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
         if (variant == 0)
-            variant = features == 128 ? 2 : 3;
+            variant = tcc::kDefaultVariant;
         *grid = *threads = *smem = 0;
         *occupancy = 0;
         auto persistent = [&](auto layout, uint32_t g) {

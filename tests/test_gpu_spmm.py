@@ -116,6 +116,23 @@ def test_misaligned_packed_x_uses_generic_path():
     assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, "misaligned packedX")
 
 
+@pytest.mark.parametrize("features", [128, 256])
+def test_ids_and_metadata_only_4_byte_aligned(features):
+    """IDs/metadata that are not 16-byte aligned (allowed by the reference's contract) take
+    the kernel without bulk copies; results stay within the bound."""
+    torch = _torch()
+    case = build_case(random_csr(600, 900, 9.0, 5), features, seed=3)
+    ids = torch.empty(case.dm.source_ids.numel() + 1, dtype=torch.int32, device="cuda")[1:]
+    ids.copy_(case.dm.source_ids)
+    meta = torch.empty(case.dm.source_metadata.numel() + 1, dtype=torch.int64, device="cuda")[1:]
+    meta.copy_(case.dm.source_metadata)
+    case.dm.source_ids, case.dm.source_metadata = ids, meta
+    y = run_spmm(case)
+    torch.cuda.synchronize()
+    y_ref, bound = oracle_y(case)
+    assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, "4-byte aligned IDs/metadata")
+
+
 def test_bad_feature_count_raises_invalid_argument():
     torch = _torch()
     case = build_case(random_csr(64, 64, 4.0, 1), 128)
