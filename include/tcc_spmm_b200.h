@@ -108,6 +108,20 @@ int tcc_quantize_pack_features_int8(const float* x, int8_t* packed, float* scale
 int tcc_spmm_workspace_size(uint32_t rows, uint32_t partial_count, uint32_t features,
                             uint64_t* partial_floats, uint64_t* counter_words);
 
+/* tcc_launch_spmm_int8 without a caller-provided workspace: the split-window partials and
+ * counters live in a static device scratch of this library (8 MiB of partials, i.e.
+ * partial_count * 8 * features <= 2^21 floats, and 1 MiB of counters, i.e.
+ * ceil(rows / 32) * features / 128 <= 2^18 words); larger needs return
+ * TCC_INVALID_ARGUMENT. The library allocates nothing: the first call on a device looks up
+ * the scratch's address (do it before any stream capture). The counters start at zero and
+ * every completed call leaves them at zero. Calls on one device share the scratch, so they
+ * must not overlap (serialise them on one stream). No counterpart in the reference, whose
+ * launchSpmmInt8 always takes the caller's SpmmWorkspace (include/spmm.cuh:10-23). */
+int tcc_launch_spmm_int8_static_workspace(const tcc_sw32_device_view* matrix, const int8_t* packed_x,
+                                          const float* scales, float* output, uint32_t rows,
+                                          uint32_t cols, uint32_t features, uint32_t partial_count,
+                                          tcc_stream_t stream);
+
 /* Status word written by bounded device waits of the SpMM kernel on the current device:
  * 0 = no wait ran out since the last reset. Synchronises the device. */
 int tcc_device_status(uint32_t* status, int reset);

@@ -95,6 +95,9 @@ SIGNATURES = {
                                                   C.c_void_p]),
     "tcc_spmm_workspace_size": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, u64p, u64p]),
     "tcc_device_status": (C.c_int, [u32p, C.c_int]),
+    "tcc_launch_spmm_int8_static_workspace": (C.c_int, [C.POINTER(Sw32DeviceView), C.c_void_p, C.c_void_p, C.c_void_p,
+                                                        C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                                        C.c_void_p]),
     "tcc_spmm_launch_shape": (C.c_int, [C.c_uint32, C.c_int, u32p, u32p, u32p, C.POINTER(C.c_int)]),
     "tcc_make_canonical_csr": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, u32p, u32p, f32p,
                                          C.POINTER(C.c_void_p)]),

@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <cuda_runtime.h>
 #include <mutex>
+#include <string>
 
 namespace tcc {
 namespace {
@@ -196,10 +197,68 @@ void launchChecked(const tcc_sw32_device_view* matrix, const int8_t* packedX, co
         launch<256>(*matrix, packedX, scales, output, rows, cols, partials, counters, stream, variant);
 }
 
+// ---- static split-window workspace (tcc_launch_spmm_int8_static_workspace) ---------------
+// File-scope device scratch for callers that cannot allocate the partial/counter workspace.
+// Zero at module load; every completed launch returns the counters to zero.
+constexpr uint64_t kStaticPartialFloats = 2ull << 20; // 8 MiB: partialCount * 8 * features floats
+constexpr uint64_t kStaticCounterWords = 1ull << 18;  // 1 MiB: ceil(rows / 32) * features / 128 words
+static __device__ __align__(256) float gStaticPartials[kStaticPartialFloats];
+static __device__ __align__(256) uint32_t gStaticCounters[kStaticCounterWords];
+
+struct StaticWorkspace {
+    float* partials = nullptr;
+    uint32_t* counters = nullptr;
+};
+
+// Device addresses of the static scratch on the current device, looked up once per device
+// (the first call on a device does this setup).
+StaticWorkspace staticWorkspace() {
+    static std::mutex mutex;
+    static StaticWorkspace cache[64];
+    int device = 0;
+    throwIf(cudaGetDevice(&device));
+    if (device < 0 || device >= 64)
+        throw CudaError("device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mutex);
+    StaticWorkspace& w = cache[device];
+    if (w.partials == nullptr) {
+        void* p = nullptr;
+        void* c = nullptr;
+        throwIf(cudaGetSymbolAddress(&p, gStaticPartials));
+        throwIf(cudaGetSymbolAddress(&c, gStaticCounters));
+        w.partials = static_cast<float*>(p);
+        w.counters = static_cast<uint32_t*>(c);
+    }
+    return w;
+}
+
 } // namespace
 } // namespace tcc
 
 extern "C" {
+
+int tcc_launch_spmm_int8_static_workspace(const tcc_sw32_device_view* matrix, const int8_t* packed_x,
+                                          const float* scales, float* output, uint32_t rows, uint32_t cols,
+                                          uint32_t features, uint32_t partial_count, tcc_stream_t stream) {
+    return tcc::guarded([&] {
+        if (features != 128 && features != 256)
+            throw std::invalid_argument("feature dimension must be 128 or 256");
+        const uint64_t partialFloats = uint64_t(partial_count) * 8 * features;
+        const uint64_t counterWords = partial_count ? (uint64_t(rows) + 31) / 32 * (features / 128) : 0;
+        if (partialFloats > tcc::kStaticPartialFloats)
+            throw std::invalid_argument("split-window partials need " + std::to_string(partialFloats * 4) +
+                                        " bytes; the static workspace holds " +
+                                        std::to_string(tcc::kStaticPartialFloats * 4));
+        if (counterWords > tcc::kStaticCounterWords)
+            throw std::invalid_argument("split-window counters need " + std::to_string(counterWords * 4) +
+                                        " bytes; the static workspace holds " +
+                                        std::to_string(tcc::kStaticCounterWords * 4));
+        const tcc::StaticWorkspace w = tcc::staticWorkspace();
+        tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features,
+                           partial_count ? w.partials : nullptr, partial_count ? w.counters : nullptr,
+                           reinterpret_cast<cudaStream_t>(stream), 0);
+    });
+}
 
 int tcc_launch_spmm_int8(const tcc_sw32_device_view* matrix, const int8_t* packed_x, const float* scales,
                          float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,

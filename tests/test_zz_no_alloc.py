@@ -1,0 +1,61 @@
+"""tcc_launch_spmm_int8_static_workspace: the SpMM with the split-window workspace in the
+library's static device scratch (no allocation by caller or library), called through the C
+ABI and compared with tcc_launch_spmm_int8 on two calls in a row. Collected last on purpose:
+it must pass both alone and after every other test has used the device."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import tcc_spmm_b200 as T
+import tcc_spmm_b200._native as N
+from tests.cases import EDGE_CASES
+from tests.conftest import assert_within_tf32_bound
+from tests.gpu_util import build_case, oracle_y
+
+pytestmark = pytest.mark.gpu
+
+
+def _static_call(case, y) -> int:
+    import torch
+
+    view = case.dm.view()
+    return N.lib().tcc_launch_spmm_int8_static_workspace(
+        C.byref(view), case.packed_dev.data_ptr(), case.scales_dev.data_ptr(), y.data_ptr(), case.fmt.rows,
+        case.fmt.cols, case.features, case.fmt.partial_count, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("features", [128, 256])
+@pytest.mark.parametrize("name", ["split_769", "split_385", "random_local"])
+def test_static_workspace_matches_caller_workspace(name, features):
+    import torch
+
+    case = build_case(EDGE_CASES[name](), features, seed=5)
+    y_ref = torch.full((case.fmt.rows, features), float("nan"), device="cuda")
+    T.launch_spmm_int8(case.dm.view(), case.packed_dev, case.scales_dev, y_ref, case.fmt.rows, case.fmt.cols,
+                       features, case.dm.workspace())
+    oracle, bound = oracle_y(case)
+    for _ in range(2):  # the second call finds the counters back at zero
+        y = torch.full_like(y_ref, float("nan"))
+        assert _static_call(case, y) == 0, T.api.N.lib().tcc_last_error()
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert_within_tf32_bound(got, y_ref.cpu().numpy(), 2 * bound, f"{name}/F{features} vs caller workspace")
+        assert_within_tf32_bound(got, oracle, bound, f"{name}/F{features} vs oracle")
+    assert T.device_status() == 0
+
+
+def test_static_workspace_rejects_oversized_partials():
+    import torch
+
+    case = build_case(EDGE_CASES["split_769"](), 128, seed=5)
+    y = torch.empty((case.fmt.rows, 128), device="cuda")
+    view = case.dm.view()
+    status = N.lib().tcc_launch_spmm_int8_static_workspace(
+        C.byref(view), case.packed_dev.data_ptr(), case.scales_dev.data_ptr(), y.data_ptr(), case.fmt.rows,
+        case.fmt.cols, 128, 1 << 20, torch.cuda.current_stream().cuda_stream)
+    assert status == 1  # TCC_INVALID_ARGUMENT
+    assert b"static workspace" in N.lib().tcc_last_error()
