@@ -336,7 +336,9 @@ def run_tcc(args):
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+        # Short enough that ranks waiting for a failed peer end with an error, long enough for
+        # the host-side matrix generation and conversion that precede the first collective.
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
     threads = max(1, host_threads() // world)
     cfg = W.CONFIGS[args.config]
     F = cfg.features
