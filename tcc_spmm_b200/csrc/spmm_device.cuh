@@ -203,22 +203,6 @@ __device__ __forceinline__ void fenceBarrierInit() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Dequantize byte K (K = 0..3) of two source words at once: the packed f32x2 pair holds
-// source a's and source b's byte, scale2 = (scale_a, scale_b). The words are already flipped
-// to unsigned bytes (word ^ 0x80808080). Same arithmetic as dequant4, biased TF32 results
-// (the tensor core drops the low 13 bits).
-template <int K>
-__device__ __forceinline__ void dequantPair(uint32_t wa, uint32_t wb, unsigned long long scale2, uint32_t& outA,
-                                            uint32_t& outB) {
-    const uint32_t magic = 0x4B000000u;
-    const unsigned long long bias2 = 0xCB000080CB000080ull; // (-8388736.f, -8388736.f)
-    const unsigned long long p = (static_cast<unsigned long long>(__byte_perm(wb, magic, 0x7540 + K)) << 32) |
-                                 __byte_perm(wa, magic, 0x7540 + K);
-    const unsigned long long f = mul2(add2(p, bias2), scale2);
-    outA = lo32(f) + 0x1000u;
-    outB = hi32(f) + 0x1000u;
-}
-
 // ---- tensor memory and the 5th-generation tensor core (tcgen05) ---------------------------
 // Allocate `cols` TMEM columns (power of two >= 32) for this CTA; the whole warp executes it
 // and the TMEM address is written to shared memory at `dst`.
@@ -250,20 +234,31 @@ __device__ __forceinline__ void tcStore16x256bx4(uint32_t taddr, const uint32_t 
                  "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
                  : "memory");
 }
-// Warp load of 32 TMEM lanes x 32 columns (32x32b shape, 32 repetitions): thread t reads
+// Warp load of 32 TMEM lanes x 16 columns (32x32b shape, 16 repetitions): thread t reads
 // lane t, r[j] = column j.
-__device__ __forceinline__ void tcLoad32x32bx32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+__device__ __forceinline__ void tcLoad32x32bx16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
                    "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                   "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                   "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-                   "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                   "=r"(r[15])
                  : "r"(taddr)
                  : "memory");
 }
+// Byte K (K = 0..3) of two source words as exact floats: the packed f32x2 pair holds
+// float(q) of source a's and source b's byte. The words are already flipped to unsigned
+// bytes (word ^ 0x80808080); every int8 is exactly representable in TF32.
+template <int K>
+__device__ __forceinline__ void int8PairToFloat(uint32_t wa, uint32_t wb, uint32_t& outA, uint32_t& outB) {
+    const uint32_t magic = 0x4B000000u;
+    const unsigned long long bias2 = 0xCB000080CB000080ull; // (-8388736.f, -8388736.f)
+    const unsigned long long p = (static_cast<unsigned long long>(__byte_perm(wb, magic, 0x7540 + K)) << 32) |
+                                 __byte_perm(wa, magic, 0x7540 + K);
+    const unsigned long long f = add2(p, bias2);
+    outA = lo32(f);
+    outB = hi32(f);
+}
+
 // D(tmem, M x N, FP32) (+)= A(tmem, M x K, TF32, K-major) * B(smem descriptor, K x N, TF32),
 // one CTA, issued by a single thread. accumulate == 0 overwrites D.
 __device__ __forceinline__ void mmaTf32Ts(uint32_t dTmem, uint32_t aTmem, unsigned long long bDesc, uint32_t idesc,

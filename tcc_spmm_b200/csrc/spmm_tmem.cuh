@@ -2,28 +2,30 @@
 // spmm_persistent.cuh with the tile product moved to the 5th-generation tensor core.
 //
 // Per panel (8 source slots x the 32 rows of a window) and 128-feature slice the CTA issues ONE
-//     tcgen05.mma.kind::tf32  D[128 features x 32 rows] += A[128 x 8 sources] * B[8 x 32]
+//     tcgen05.mma.kind::tf32  D[128 features x 64] += A[128 x 8 sources] * B[8 x 64]
 // with
-//   A  the dequantized feature rows (X^T), written straight into tensor memory by the consumer
-//      warps (tcgen05.st) - no shared-memory round trip and no register accumulators;
-//   B  the panel's TF32 values as a dense K-major 8 x 32 tile in shared memory, built by a
-//      producer warp (zero fill plus a scatter of the panel's nonzeros);
-//   D  an FP32 accumulator of the window in tensor memory, double-buffered so the epilogue of
-//      one window (tcgen05.ld -> Y or the partial blocks) overlaps the next window's MMAs.
-// The reference computes the same products per warp with mma.sync
-// (src/kernel/spmm_kernel.cuh:77-90,131-169); the arithmetic per term is the same:
-// tf32_rna(a) * tf32_rna(float(q) * scale), accumulated in FP32.
+//   A  the INT8 feature bytes of the 8 source rows as exact floats (X^T; every int8 is a TF32
+//      value), written straight into tensor memory by the consumer warps (tcgen05.st);
+//   B  the panel's values with the per-source scale folded in, b = tf32(a) * scale, as a dense
+//      K-major tile in shared memory: columns 0-31 hold tf32(b) and columns 32-63 the TF32
+//      remainder tf32(b - tf32(b)), so hi + lo carries b to 22 significant bits. A producer warp
+//      builds it (zero fill plus a scatter of the panel's nonzeros);
+//   D  the window's FP32 accumulator in tensor memory; Y row j = D[:, j] + D[:, 32 + j].
+// Every product the tensor core forms is exact, so each term is q * tf32(a) * scale to 22 bits:
+// within 2^-11 relative of the reference's tf32_rna(a) * tf32_rna(float(q) * scale)
+// (src/kernel/spmm_kernel.cuh:7-19,45-57), half its stated bound; the scale multiply moves
+// from 1024 feature values per panel to the panel's few nonzeros.
 //
 // Warp roles (the chunks - 4 panels, 32 source slots - of the CTA's tasks b, b+G, ... form one
 // stream; producer pw owns chunks pw, pw+P, ... and every ring slot they map to):
 //   consumers 0..F/32-1  warp w owns TMEM lane quarter w%4 of slice w/4 (32 features). X step
 //                        (kPrefetch chunks ahead): cp.async of its 32 bytes of the chunk's 32
 //                        packed source rows (L2 evict-last: rows are shared by neighbouring
-//                        windows). Then it dequantizes them into the stage's A columns.
+//                        windows). Then it converts them to floats in the stage's A columns.
 //   producers (P warps)  A step  (kALead ahead): bulk copies (TMA engine) of the chunk's 32
 //                                source IDs and metadata words;
 //                        V step  (kVLead ahead): cp.async of the value range and 32 scales;
-//                        B step  the stage's B tiles and scales, then publish the stage.
+//                        B step  the stage's B tiles (values times scales), then publish it.
 //   MMA warp             one thread issues the MMAs of each chunk and the commits.
 //
 // Feature order inside a consumer's TMEM lane quarter: lane l holds feature
@@ -35,13 +37,14 @@
 //   aLand[a]  A step bulk copies -> all     : IDs and metadata of the chunk landed
 //   aUsed[a]  consumers -> producer         : IDs read (X step issued), the slot may be refilled
 //   vFull[v]  V step cp.async -> producer   : values and scales landed
-//   bFull[s]  producer -> consumers         : B tiles and scales of stage s written
+//   bFull[s]  producer -> consumers         : B tiles of stage s written
 //   aFull[s]  consumers -> MMA              : A columns of stage s stored (implies bFull[s])
 //   sFree[s]  MMA commit -> producer        : the MMAs reading stage s are complete; the
 //                                             producer's next bFull[s] passes this on to the
 //                                             consumers (their A columns are free again)
-//   dFull[d]  MMA commit -> consumers       : accumulator d holds the window's result
-//   dFree[d]  consumers -> MMA              : accumulator d has been read
+//   dFull     MMA commit -> consumers       : the accumulator holds the window's result
+//   dFree     consumers -> MMA              : the accumulator has been read (the next window's
+//                                             first MMA overwrites it)
 #pragma once
 #include "spmm_persistent.cuh"
 
@@ -68,22 +71,23 @@ template <int F, int STAGES, int P> struct Tmem {
     static constexpr int kVCap = 128;
     static constexpr int kASlotBytes = 128 + 256 + 16; // ids, metadata, header (p0, np)
     static constexpr int kVSlotBytes = kVCap * 4 + 128; // values, scales
-    // Stage: four B tiles (one per panel, 32 rows x 8 sources TF32, K-major core matrices:
-    // element (row r, source k) at (r%8)*16 + (r/8)*256 + (k/4)*128 + (k%4)*4) + 32 scales.
-    static constexpr int kBTileBytes = 1024;
+    // Stage: four B tiles (one per panel, 64 columns x 8 sources TF32, K-major core matrices:
+    // element (column n, source k) at (n%8)*16 + (n/8)*256 + (k/4)*128 + (k%4)*4).
+    static constexpr int kBTileBytes = 2048;
     static constexpr int kBOff = 0;
-    static constexpr int kScaleOff = kBOff + kStages * kChunk * kBTileBytes;
-    static constexpr int kXOff = kScaleOff + kStages * 128;
+    static constexpr int kXOff = kBOff + kStages * kChunk * kBTileBytes;
     static constexpr int kAOff = kXOff + kConsumers * kXDepth * kXSlotBytes;
     static constexpr int kVOff = kAOff + kARing * kASlotBytes;
     static constexpr int kVBaseOff = kVOff + kVRing * kVSlotBytes;
     static constexpr int kFlagOff = kVBaseOff + 32;
     static constexpr int kBarOff = kFlagOff + 16;
-    // bFull, aFull, sFree [kStages]; dFull, dFree [2]; aLand, aUsed [kARing]; vFull [kVRing]; drain
+    // bFull, aFull, sFree [kStages]; dFull, dFree (two words reserved each); aLand, aUsed
+    // [kARing]; vFull [kVRing]; drain
     static constexpr int kBars = 3 * kStages + 4 + 2 * kARing + kVRing + 1;
     static constexpr int kBytes = kBarOff + 8 * kBars;
-    // Tensor memory: per slice, kStages A slots of 32 columns (4 panels x 8 sources) and two
-    // accumulators of 32 columns (the window's rows); allocation is a power of two.
+    // Tensor memory: per slice, kStages A slots of 32 columns (4 panels x 8 sources) and the
+    // accumulator of 64 columns (hi and lo products of the window's 32 rows); allocation is a
+    // power of two.
     static constexpr int kSliceCols = 32 * kStages + 64;
     static constexpr int kColsUsed = kSlices * kSliceCols;
     static constexpr int kTmemCols = kColsUsed <= 32    ? 32
@@ -101,8 +105,8 @@ template <int F, int STAGES, int P> struct Tmem {
                   "power-of-two rings");
     static_assert(kXOff % 16 == 0 && kAOff % 16 == 0 && kVOff % 16 == 0 && kBarOff % 8 == 0, "alignment");
     // Instruction descriptor: D FP32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2), both
-    // K-major, N = 32 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16).
-    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+    // K-major, N = 64 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16).
+    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 };
 
 // Shared-memory matrix descriptor of one B tile (no swizzle, K-major core matrices of 8 rows
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
             }
             if (!ok)
                 break;
-            // ---- B step: B tiles and scales of chunk seqF; publish the stage ----
+            // ---- B step: B tiles of chunk seqF; publish the stage ----
             const uint32_t aslot = seqF % L::kARing, vslot = seqF % L::kVRing, stage = seqF % L::kStages;
             if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1) ||
                 (seqF >= uint32_t(L::kStages) &&
@@ -288,8 +292,7 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
             const unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
             const uint32_t np = reinterpret_cast<const uint32_t*>(a + 384)[1];
             unsigned char* tiles = smem + L::kBOff + stage * (kChunk * L::kBTileBytes);
-            reinterpret_cast<float*>(smem + L::kScaleOff + stage * 128)[lane] =
-                reinterpret_cast<const float*>(v + 4 * L::kVCap)[lane];
+            const float scale = reinterpret_cast<const float*>(v + 4 * L::kVCap)[lane];
             {
                 uint4* z = reinterpret_cast<uint4*>(tiles);
 #pragma unroll
@@ -309,7 +312,13 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                 mask &= mask - 1;
                 const float value = vb != 0xFFFFFFFFu ? vsm[first + j - vb] : __ldg(matrix.values + first + j);
                 ++j;
-                tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = dev::tf32Exact(value);
+                // b = tf32(a) * scale as a TF32 pair hi + lo (22 significant bits): rows 0-31
+                // of the tile hold hi, rows 32-63 lo.
+                const float b = __uint_as_float(dev::tf32Exact(value)) * scale;
+                const uint32_t hi = dev::tf32Exact(b);
+                const uint32_t lo = dev::tf32Exact(b - __uint_as_float(hi));
+                tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = hi;
+                tile[((r & 7) * 16 + (r >> 3) * 256 + 1024) / 4] = lo;
             }
             dev::fenceProxyAsyncShared();
             __syncwarp();
@@ -333,8 +342,9 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                 const uint32_t panelCount = task.end - task.begin;
                 if (panelCount == 0)
                     continue;
-                const uint32_t d = windows & 1;
-                if (ok && windows >= 2 && !boundedWaitBackoff(barR + 8 * d, ((windows >> 1) - 1) & 1))
+                // One accumulator (64 columns): the window's first MMA overwrites it once the
+                // consumers have read the previous window's result.
+                if (ok && windows >= 1 && !boundedWaitBackoff(barR, (windows - 1) & 1))
                     ok = false;
                 ++windows;
                 dev::tcFenceAfter();
@@ -353,7 +363,7 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                         const unsigned long long desc = bTileDesc(tiles + pp * L::kBTileBytes);
 #pragma unroll
                         for (int sl = 0; sl < L::kSlices; ++sl)
-                            dev::mmaTf32Ts(tmem + sl * L::kSliceCols + 32 * L::kStages + 32 * d,
+                            dev::mmaTf32Ts(tmem + sl * L::kSliceCols + 32 * L::kStages,
                                            tmem + sl * L::kSliceCols + 32 * stage + 8 * pp, desc, L::kIdesc,
                                            (ch | pp) != 0);
                     }
@@ -361,7 +371,7 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                     dev::tcCommit(barS + 8 * stage);
                 }
                 if (ok)
-                    dev::tcCommit(barD + 8 * d);
+                    dev::tcCommit(barD);
             }
             if (issued) { // every MMA is complete before the tensor memory is released
                 dev::tcCommit(barF);
@@ -410,17 +420,15 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                     continue;
                 dev::tcFenceAfter();
                 const uint32_t xs = xLane + (seq & (L::kXDepth - 1)) * L::kXSlotBytes;
-                const uint32_t sc = base + L::kScaleOff + stage * 128 + 8 * c;
                 uint32_t lo[16], hi[16];
 #pragma unroll
                 for (int pp = 0; pp < kChunk; ++pp) {
-                    const unsigned long long s2 = dev::ldsU64(sc + 32 * pp); // scales of sources 2c, 2c+1
                     const uint32_t wa = dev::ldsU32(xs + 8 * pp * L::kXRowStride) ^ 0x80808080u;
                     const uint32_t wb = dev::ldsU32(xs + (8 * pp + 1) * L::kXRowStride) ^ 0x80808080u;
-                    dev::dequantPair<0>(wa, wb, s2, lo[4 * pp + 0], lo[4 * pp + 1]);
-                    dev::dequantPair<1>(wa, wb, s2, lo[4 * pp + 2], lo[4 * pp + 3]);
-                    dev::dequantPair<2>(wa, wb, s2, hi[4 * pp + 0], hi[4 * pp + 1]);
-                    dev::dequantPair<3>(wa, wb, s2, hi[4 * pp + 2], hi[4 * pp + 3]);
+                    dev::int8PairToFloat<0>(wa, wb, lo[4 * pp + 0], lo[4 * pp + 1]);
+                    dev::int8PairToFloat<1>(wa, wb, lo[4 * pp + 2], lo[4 * pp + 3]);
+                    dev::int8PairToFloat<2>(wa, wb, hi[4 * pp + 0], hi[4 * pp + 1]);
+                    dev::int8PairToFloat<3>(wa, wb, hi[4 * pp + 2], hi[4 * pp + 3]);
                 }
                 dev::tcStore16x256bx4(aTmem + 32 * stage, lo);
                 dev::tcStore16x256bx4(aTmem + 32 * stage + (16u << 16), hi);
@@ -431,53 +439,59 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
                     dev::mbarArrive(barA + 8 * stage);
             }
             // ---- epilogue of this window ----
-            uint32_t acc[32];
-            if (panelCount > 0) {
-                const uint32_t d = windows & 1;
-                if (ok && !boundedWait(barD + 8 * d, (windows >> 1) & 1))
-                    ok = false;
-                ++windows;
-                if (ok) {
-                    dev::tcFenceAfter();
-                    dev::tcLoad32x32bx32(dTmem + 32 * d, acc);
-                    dev::tcWaitLd();
-                    dev::tcFenceBefore();
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        acc[j] = 0u;
-                }
-                __syncwarp();
-                if (lane == 0)
-                    dev::mbarArrive(barR + 8 * d);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    acc[j] = 0u;
-            }
             const uint32_t rowBase = task.sw * 32;
             const bool split = task.partial != kNoPartial;
-            if (split && (partials == nullptr || counters == nullptr)) {
-                if (threadIdx.x == 0)
-                    atomicOr(&gDeviceStatus, 2u);
-                continue;
+            const bool haveWs = !split || (partials != nullptr && counters != nullptr);
+            if (!haveWs && threadIdx.x == 0)
+                atomicOr(&gDeviceStatus, 2u);
+            bool loaded = false;
+            if (panelCount > 0) {
+                if (ok && !boundedWait(barD, windows & 1))
+                    ok = false;
+                ++windows;
+                loaded = ok;
+                if (loaded)
+                    dev::tcFenceAfter();
             }
-            if (!split) {
+            // Y row j = column j (the hi products) + column 32 + j (the lo products), stored 16
+            // rows at a time: straight to Y, or to the split task's partial block of the row's
+            // 8-row group.
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (rowBase + j < rows)
-                        __stcs(output + uint64_t(rowBase + j) * F + feature, __uint_as_float(acc[j]));
-                continue;
-            }
+            for (int half = 0; half < 2; ++half) {
+                uint32_t h[16], l[16];
+                if (loaded) {
+                    dev::tcLoad32x32bx16(dTmem + 16 * half, h);
+                    dev::tcLoad32x32bx16(dTmem + 32 + 16 * half, l);
+                    dev::tcWaitLd();
+                } else {
 #pragma unroll
-            for (int rw = 0; rw < 4; ++rw) {
-                if (!(task.mask & (1u << rw)))
+                    for (int j = 0; j < 16; ++j)
+                        h[j] = l[j] = 0u;
+                }
+                if (!haveWs)
                     continue;
-                const uint64_t block = task.partial + __popc(task.mask & ((1u << rw) - 1));
 #pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    __stcg(partials + (block * 8 + r) * F + feature, __uint_as_float(acc[8 * rw + r]));
+                for (int j = 0; j < 16; ++j) {
+                    const int row = 16 * half + j;
+                    const float y = __uint_as_float(h[j]) + __uint_as_float(l[j]);
+                    if (!split) {
+                        if (rowBase + row < rows)
+                            __stcs(output + uint64_t(rowBase + row) * F + feature, y);
+                    } else if (task.mask & (1u << (row >> 3))) {
+                        const uint64_t block = task.partial + __popc(task.mask & ((1u << (row >> 3)) - 1));
+                        __stcg(partials + (block * 8 + (row & 7)) * F + feature, y);
+                    }
+                }
             }
+            if (panelCount > 0) {
+                if (loaded)
+                    dev::tcFenceBefore();
+                __syncwarp();
+                if (lane == 0)
+                    dev::mbarArrive(barR);
+            }
+            if (!split || !haveWs)
+                continue;
             // Last-arriver merge among the consumer warps (reference src/kernel/spmm_kernel.cuh:250-282).
             __threadfence();
             namedBarrier(1, 32 * L::kConsumers);
