@@ -51,6 +51,7 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-slices", type=int, default=8, help="window-aligned task slices per end-to-end step")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-gpu-format", action="store_true", help="skip timing the GPU SW32 construction")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
                             "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"],
@@ -272,6 +273,30 @@ def build_workload(config: str, threads: int, use_reference_format: bool = False
     return csr, fmt, {"generate_s": round(t1 - t0, 2), "convert_s": round(t2 - t1, 2)}
 
 
+def time_gpu_format(T, csr, fmt, device, repeats: int = 3) -> dict:
+    """The SW32 format and task plan built on this GPU from the CSR (not part of the metric):
+    wall time of tcc_convert_csr_to_sw32_device (it synchronises to size its outputs), median
+    of `repeats` after one untimed call, and whether every array equals the host builder's."""
+    import torch
+
+    def up(a, dtype):
+        return torch.from_numpy(np.ascontiguousarray(a).view(dtype)).to(device)
+
+    ro, si, va = up(csr.row_offsets, np.int32), up(csr.source_ids, np.int32), up(csr.values, np.float32)
+    T.convert_csr_to_sw32_device(csr.rows, csr.cols, ro, si, va)
+    times = []
+    for _ in range(repeats):
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        dev = T.convert_csr_to_sw32_device(csr.rows, csr.cols, ro, si, va)
+        torch.cuda.synchronize(device)
+        times.append(time.perf_counter() - t0)
+    identical = not dev.differences(fmt)
+    del dev, ro, si, va
+    torch.cuda.empty_cache()
+    return {"gpu_convert_ms": round(1e3 * sorted(times)[len(times) // 2], 2), "identical_to_host": identical}
+
+
 def cpu_sample(fmt, features: int, target_seconds: float, threads: int, seed: int = 1):
     """Windows of a strided sample and their nnz, sized to about target_seconds of oracle work."""
     import oracle as O
@@ -417,6 +442,9 @@ def run_tcc(args):
                "sample": f"every {stride}th 32-row window ({sample.size} windows, {snnz} nnz) of {args.config}, "
                          f"oracle/tcc_oracle.c restatement of the reference arithmetic, {t:.2f} s",
                "seconds": round(t, 3), "threads_reported": O.max_threads()}
+
+    if not args.no_gpu_format:
+        prep.update(time_gpu_format(T, csr, fmt, device))
 
     if world > 1:
         dist.barrier(device_ids=[local])

@@ -187,6 +187,35 @@ int tcc_sw32_host_sizes(const tcc_sw32_host* host, tcc_sw32_sizes* sizes);
 int tcc_sw32_host_arrays(const tcc_sw32_host* host, tcc_sw32_arrays* arrays);
 void tcc_sw32_host_free(tcc_sw32_host* host);
 
+/* ---------------------------------------------------------------------------------
+ * Device format construction
+ * --------------------------------------------------------------------------------- */
+
+/* SW32 format built on the GPU, owned by the library (one device allocation). */
+typedef struct tcc_sw32_device tcc_sw32_device;
+
+/* convertCsrToSw32 (reference include/format/sw32.h:66-67, src/format/sw32.cpp:69-167) and
+ * buildPanelTasks (src/format/sw32.cpp:25-65) on the current device, from a canonical CSR
+ * whose row_offsets (rows + 1), source_ids and values (nnz each) are device pointers. The
+ * arrays are byte-identical to tcc_convert_csr_to_sw32's, and invalid input gives the same
+ * status and message. No reference counterpart: the reference builds the format on the host
+ * only. Unlike the launch entry points this call allocates device memory (the output, and
+ * stream-ordered scratch of about 40 bytes per nonzero that is released in stream order
+ * before it returns) and synchronises `stream` a few times to read sizes; the arrays are
+ * ready for work enqueued on `stream` after it returns. */
+int tcc_convert_csr_to_sw32_device(uint32_t rows, uint32_t cols, const uint32_t* row_offsets,
+                                   const uint32_t* source_ids, const float* values, uint64_t nnz,
+                                   int bucket_by_rw_mask, tcc_stream_t stream, tcc_sw32_device** out);
+/* Sizes and device pointers of the built arrays (valid until tcc_sw32_device_free). Every
+ * pointer is non-null, also for an empty array. */
+int tcc_sw32_device_sizes(const tcc_sw32_device* format, tcc_sw32_sizes* sizes);
+int tcc_sw32_device_arrays(const tcc_sw32_device* format, tcc_sw32_arrays* arrays);
+/* The device view of all tasks, as an upload would give it (reference
+ * src/device_matrix.cuh:8-37 builds the same view from its uploaded arrays). */
+int tcc_sw32_device_view_of(const tcc_sw32_device* format, tcc_sw32_device_view* view);
+/* Frees the arrays (synchronises the device). */
+void tcc_sw32_device_free(tcc_sw32_device* format);
+
 /* Multi-GPU sharding (no reference counterpart; the reference is single-GPU): cut the
  * task array into `parts` contiguous ranges at SW boundaries with balanced estimated cost
  * (panels, active row-group MMAs and the per-task write-back). bounds gets parts+1 task

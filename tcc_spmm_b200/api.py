@@ -4,7 +4,8 @@ Reference (Shixg-cnic/tcc_spmm)            this module
 -----------------------------------------  ----------------------------------------------
 makeCanonicalCsr   include/format/csr.h:23  make_canonical_csr
 loadMatrixMarket   include/format/csr.h:18  load_matrix_market
-convertCsrToSw32   include/format/sw32.h:66 convert_csr_to_sw32 (includes buildPanelTasks)
+convertCsrToSw32   include/format/sw32.h:66 convert_csr_to_sw32 (includes buildPanelTasks);
+                                            convert_csr_to_sw32_device builds it on the GPU
 Sw32HostFormat     include/format/sw32.h:45 Sw32HostFormat
 DeviceMatrix       src/device_matrix.cuh:8  DeviceMatrix (view(), workspace())
 SpmmWorkspace      include/spmm.cuh:10      SpmmWorkspace
@@ -320,6 +321,25 @@ class DeviceMatrix:
                                 self.tasks.data_ptr() + TASK_DTYPE.itemsize * first, self.reductions.data_ptr(),
                                 self.partial_ids.data_ptr(), last - first)
 
+    @classmethod
+    def from_device_format(cls, fmt: "Sw32DeviceFormat", features: int) -> "DeviceMatrix":
+        """A DeviceMatrix over a format built on the GPU (no upload): the arrays are the
+        library's; only the workspace for `features` is allocated here."""
+        import torch
+
+        self = cls.__new__(cls)
+        self.rows, self.cols, self.features = fmt.rows, fmt.cols, features
+        self.device = fmt.window_offsets.device
+        for name in ("window_offsets", "source_ids", "row_group_masks", "source_metadata", "values",
+                     "bucket_offsets", "tasks", "reductions", "partial_ids"):
+            setattr(self, name, getattr(fmt, name))
+        self.task_count, self.partial_count = fmt.task_count, fmt.partial_count
+        self._format = fmt
+        pf, cw = workspace_size(fmt.rows, fmt.partial_count, features)
+        self.partials = torch.empty(pf, dtype=torch.float32, device=self.device) if pf else None
+        self.counters = torch.zeros(cw, dtype=torch.int32, device=self.device) if cw else None
+        return self
+
     def workspace(self) -> SpmmWorkspace:
         return SpmmWorkspace(self.partials, self.counters)
 
@@ -327,6 +347,120 @@ class DeviceMatrix:
         ts = [self.window_offsets, self.source_ids, self.row_group_masks, self.source_metadata, self.values,
               self.bucket_offsets, self.tasks, self.reductions, self.partial_ids, self.partials, self.counters]
         return sum(t.numel() * t.element_size() for t in ts if t is not None)
+
+
+class _LibraryArray:
+    """A device array owned by a library handle, exposed through __cuda_array_interface__
+    (torch.as_tensor keeps this object, and so the handle, alive)."""
+
+    def __init__(self, ptr: int, count: int, typestr: str, owner):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+        self._owner = owner
+
+
+class _DeviceFormatHandle:
+    def __init__(self, handle: C.c_void_p):
+        self.handle = handle
+
+    def __del__(self):
+        if self.handle:
+            N.lib().tcc_sw32_device_free(self.handle)
+            self.handle = None
+
+
+@dataclass
+class Sw32DeviceFormat:
+    """SW32 format and task plan built on the GPU (tcc_convert_csr_to_sw32_device). The
+    tensors alias the library's allocation: u32 arrays as int32, metadata as int64, tasks
+    and reduce ranges flattened to int32 words. to_host() copies them into an
+    Sw32HostFormat, which compares byte for byte with convert_csr_to_sw32's."""
+
+    rows: int
+    cols: int
+    bucketed: bool
+    window_offsets: object
+    source_ids: object
+    row_group_masks: object
+    source_metadata: object
+    values: object
+    bucket_offsets: object
+    tasks: object
+    reductions: object
+    partial_ids: object
+    task_count: int
+    reduction_count: int
+    partial_count: int
+    _handle: object = field(repr=False, default=None)
+
+    def to_host(self) -> Sw32HostFormat:
+        def h(t, dtype):
+            return t.cpu().numpy().view(dtype)
+
+        return Sw32HostFormat(
+            rows=self.rows, cols=self.cols, window_offsets=h(self.window_offsets, np.uint32),
+            source_ids=h(self.source_ids, np.uint32), row_group_masks=h(self.row_group_masks, np.uint32),
+            source_metadata=h(self.source_metadata, np.uint64), values=h(self.values, np.float32),
+            bucket_offsets=h(self.bucket_offsets, np.uint32), tasks=h(self.tasks, np.uint32).view(TASK_DTYPE),
+            reductions=h(self.reductions, np.uint32).view(REDUCE_DTYPE), partial_ids=h(self.partial_ids, np.uint32),
+            partial_count=self.partial_count)
+
+    def device_matrix(self, features: int) -> "DeviceMatrix":
+        return DeviceMatrix.from_device_format(self, features)
+
+    def differences(self, host: Sw32HostFormat) -> list:
+        """Names of the arrays (and counts) that differ from `host`, compared bit for bit on the
+        device (the host arrays are uploaded one at a time)."""
+        import torch
+
+        out = [] if (self.rows, self.cols, self.partial_count) == (host.rows, host.cols, host.partial_count) \
+            else ["sizes"]
+        for name in ("window_offsets", "source_ids", "row_group_masks", "source_metadata", "values", "bucket_offsets",
+                     "tasks", "reductions", "partial_ids"):
+            mine = getattr(self, name)
+            ref = np.ascontiguousarray(getattr(host, name))
+            ref = ref.view(np.int64) if mine.dtype == torch.int64 else ref.view(np.int32)
+            mine = mine if mine.dtype == torch.int64 else mine.view(torch.int32)
+            if mine.numel() != ref.size or not torch.equal(mine, torch.from_numpy(ref).to(mine.device)):
+                out.append(name)
+        return out
+
+
+def convert_csr_to_sw32_device(rows: int, cols: int, row_offsets, source_ids, values, bucket_by_rw_mask: bool = True,
+                               stream=None) -> Sw32DeviceFormat:
+    """convertCsrToSw32 + buildPanelTasks on the GPU (reference src/format/sw32.cpp:69-167,
+    :25-65) from a canonical CSR in device memory (torch tensors of 4-byte elements on the
+    current device). Same arrays and the same errors as convert_csr_to_sw32."""
+    import torch
+
+    if row_offsets.numel() != rows + 1 or values.numel() != source_ids.numel():
+        raise InvalidArgument("invalid canonical CSR for source-mask SW32")
+    for t in (row_offsets, source_ids, values):
+        if not t.is_cuda or t.element_size() != 4 or not t.is_contiguous():
+            raise InvalidArgument("device CSR arrays must be contiguous 4-byte CUDA tensors")
+    lib = N.lib()
+    handle = C.c_void_p()
+    nnz = int(source_ids.numel())
+    _check(lib.tcc_convert_csr_to_sw32_device(rows, cols, row_offsets.data_ptr(), source_ids.data_ptr() if nnz else 0,
+                                              values.data_ptr() if nnz else 0, nnz, int(bool(bucket_by_rw_mask)),
+                                              _stream_handle(stream, row_offsets), C.byref(handle)))
+    owner = _DeviceFormatHandle(handle)
+    s, a = N.Sw32Sizes(), N.Sw32Arrays()
+    _check(lib.tcc_sw32_device_sizes(handle, C.byref(s)))
+    _check(lib.tcc_sw32_device_arrays(handle, C.byref(a)))
+
+    def t(ptr, count, typestr):
+        return torch.as_tensor(_LibraryArray(ptr, count, typestr, owner), device=row_offsets.device)
+
+    return Sw32DeviceFormat(
+        rows=s.rows, cols=s.cols, bucketed=bool(s.bucketed),
+        window_offsets=t(a.windowOffsets, s.windowOffsets, "<i4"), source_ids=t(a.sourceIds, s.sourceIds, "<i4"),
+        row_group_masks=t(a.rowGroupMasks, s.rowGroupMasks, "<i4"),
+        source_metadata=t(a.sourceMetadata, s.sourceIds, "<i8"), values=t(a.values, s.values, "<f4"),
+        bucket_offsets=t(a.bucketOffsets, s.bucketOffsets, "<i4"), tasks=t(a.tasks, 7 * s.tasks, "<i4"),
+        reductions=t(a.reductions, 2 * s.reductions, "<i4"), partial_ids=t(a.partialIds, s.partialIds, "<i4"),
+        task_count=int(s.tasks), reduction_count=int(s.reductions), partial_count=int(s.partialCount),
+        _handle=owner)
 
 
 def _np_of(torch_dtype):

@@ -25,7 +25,8 @@ CXX = os.environ.get("CXX", "g++")
 CUDA_INCLUDE = Path(NVCC).resolve().parent.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-LIB_SOURCES = ["format.cpp", "capi_host.cpp", "cxx_api.cpp", "features.cu", "spmm.cu", "matrix_market.cpp"]
+LIB_SOURCES = ["format.cpp", "capi_host.cpp", "cxx_api.cpp", "features.cu", "spmm.cu", "format_gpu.cu",
+               "matrix_market.cpp"]
 
 
 def _run(cmd: list[str]) -> None:

@@ -102,3 +102,39 @@ EDGE_CASES = {
     "single_term": lambda: single_term_csr(300, 500),
     "one_row": lambda: random_csr(1, 40, 10.0, 9),
 }
+
+
+def bad_sw32_inputs():
+    """Invalid inputs of convertCsrToSw32, one per check of the reference's merge and offsets."""
+    good = random_csr(40, 50, 4.0, 3)
+    ro, si, va = good.row_offsets.copy(), good.source_ids.copy(), good.values.copy()
+    cases = {}
+    bad = va.copy()
+    bad[3] = 0.0
+    cases["zero value"] = (40, 50, ro, si, bad)
+    bad = va.copy()
+    bad[5] = np.nan
+    cases["nan value"] = (40, 50, ro, si, bad)
+    bad = si.copy()
+    bad[2] = 50
+    cases["source out of range"] = (40, 50, ro, bad, va)
+    bad = si.copy()
+    r = int(np.argmax(np.diff(ro) >= 2))
+    bad[ro[r]], bad[ro[r] + 1] = bad[ro[r] + 1], bad[ro[r]]
+    cases["decreasing row sources"] = (40, 50, ro, bad, va)
+    bad = ro.copy()
+    bad[10], bad[11] = bad[11], bad[10]
+    if bad[10] > bad[11]:
+        cases["decreasing offsets"] = (40, 50, bad, si, va)
+    cases["zero rows"] = (0, 50, np.zeros(1, np.uint32), si[:0], va[:0])
+    cases["zero cols"] = (40, 0, ro, si, va)
+    bad = ro.copy()
+    bad[-1] -= 1
+    cases["offsets end mismatch"] = (40, 50, bad, si, va)
+    # Two failing windows: the error is the one of the first window in window order.
+    big = random_csr(200, 60, 5.0, 8)
+    bro, bsi, bva = big.row_offsets, big.source_ids.copy(), big.values.copy()
+    bva[bro[110]] = 0.0                   # window 3
+    bsi[bro[41] + 1] = 60                 # window 1: source out of range
+    cases["two bad windows"] = (200, 60, bro, bsi, bva)
+    return cases

@@ -9,7 +9,7 @@ import pytest
 import oracle as O
 import tcc_spmm_b200 as T
 from tcc_spmm_b200 import workloads as W
-from tests.cases import EDGE_CASES, random_csr
+from tests.cases import EDGE_CASES, bad_sw32_inputs, random_csr
 
 pytestmark = pytest.mark.skipif(not O.have_ref_host(), reason="oracle/_ref not built")
 
@@ -81,38 +81,9 @@ def test_split_tasks_cover_every_panel_once():
 # --------------------------------------------------------------------------------------
 # Error behaviour: same exception type and message as the reference.
 # --------------------------------------------------------------------------------------
-def _bad_inputs():
-    good = random_csr(40, 50, 4.0, 3)
-    ro, si, va = good.row_offsets.copy(), good.source_ids.copy(), good.values.copy()
-    cases = {}
-    bad = va.copy()
-    bad[3] = 0.0
-    cases["zero value"] = (40, 50, ro, si, bad)
-    bad = va.copy()
-    bad[5] = np.nan
-    cases["nan value"] = (40, 50, ro, si, bad)
-    bad = si.copy()
-    bad[2] = 50
-    cases["source out of range"] = (40, 50, ro, bad, va)
-    bad = si.copy()
-    r = int(np.argmax(np.diff(ro) >= 2))
-    bad[ro[r]], bad[ro[r] + 1] = bad[ro[r] + 1], bad[ro[r]]
-    cases["decreasing row sources"] = (40, 50, ro, bad, va)
-    bad = ro.copy()
-    bad[10], bad[11] = bad[11], bad[10]
-    if bad[10] > bad[11]:
-        cases["decreasing offsets"] = (40, 50, bad, si, va)
-    cases["zero rows"] = (0, 50, np.zeros(1, np.uint32), si[:0], va[:0])
-    cases["zero cols"] = (40, 0, ro, si, va)
-    bad = ro.copy()
-    bad[-1] -= 1
-    cases["offsets end mismatch"] = (40, 50, bad, si, va)
-    return cases
-
-
-@pytest.mark.parametrize("case", sorted(_bad_inputs()))
+@pytest.mark.parametrize("case", sorted(bad_sw32_inputs()))
 def test_invalid_input_same_error_as_reference(case):
-    rows, cols, ro, si, va = _bad_inputs()[case]
+    rows, cols, ro, si, va = bad_sw32_inputs()[case]
     with pytest.raises(O.oracle.RefError) as ref_err:
         O.ref_convert_csr_to_sw32(rows, cols, ro, si, va)
     csr = T.CsrMatrix(rows, cols, ro, si, va)

@@ -76,3 +76,19 @@ def test_full_size_properties(config, features):
     keep = rows >= 0
     got = y[torch.from_numpy(rows[keep]).cuda()].cpu().numpy()
     assert_within_tf32_bound(got, ref[keep], bound[keep])
+
+
+@pytest.mark.parametrize("config", ["powerlaw128", "stress", "rmat"])
+def test_full_size_device_format_identical(config):
+    """The GPU-built format of every full-size workload equals the host builder's, bit for bit."""
+    import torch
+
+    csr = W.generate(config)
+    fmt = T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+
+    def up(a, dtype):
+        return torch.from_numpy(np.ascontiguousarray(a).view(dtype)).cuda()
+
+    dev = T.convert_csr_to_sw32_device(csr.rows, csr.cols, up(csr.row_offsets, np.int32),
+                                       up(csr.source_ids, np.int32), up(csr.values, np.float32))
+    assert dev.differences(fmt) == []
