@@ -293,6 +293,7 @@ def time_gpu_format(T, csr, fmt, device, repeats: int = 3) -> dict:
         times.append(time.perf_counter() - t0)
     identical = not dev.differences(fmt)
     del dev, ro, si, va
+    T.sw32_device_trim()
     torch.cuda.empty_cache()
     return {"gpu_convert_ms": round(1e3 * sorted(times)[len(times) // 2], 2), "identical_to_host": identical}
 

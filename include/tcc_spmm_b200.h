@@ -8,7 +8,9 @@
  *
  * Conventions shared with the reference library (Shixg-cnic/tcc_spmm):
  *   - The caller allocates and owns every device buffer. Device entry points allocate
- *     nothing and never synchronise; they enqueue work on `stream` and return.
+ *     nothing and never synchronise; they enqueue work on `stream` and return. The one
+ *     exception is the device format builder (tcc_convert_csr_to_sw32_device), whose output
+ *     sizes depend on the data.
  *   - Sizes are 32-bit, as in the reference (rows, cols, features, nnz).
  *   - All device pointers are plain CUDA device addresses; `stream` is a cudaStream_t
  *     (NULL = legacy default stream).
@@ -199,10 +201,11 @@ typedef struct tcc_sw32_device tcc_sw32_device;
  * whose row_offsets (rows + 1), source_ids and values (nnz each) are device pointers. The
  * arrays are byte-identical to tcc_convert_csr_to_sw32's, and invalid input gives the same
  * status and message. No reference counterpart: the reference builds the format on the host
- * only. Unlike the launch entry points this call allocates device memory (the output, and
- * stream-ordered scratch of about 40 bytes per nonzero that is released in stream order
- * before it returns) and synchronises `stream` a few times to read sizes; the arrays are
- * ready for work enqueued on `stream` after it returns. */
+ * only. Unlike the launch entry points this call allocates device memory and synchronises
+ * `stream` a few times to read sizes; the arrays are ready for work enqueued on `stream` after
+ * it returns. Its memory (the output, and scratch of at most about 36 bytes per nonzero that is
+ * released in stream order before the call returns) comes from a memory pool of the library,
+ * one per device, that keeps freed memory for the next build until tcc_sw32_device_trim. */
 int tcc_convert_csr_to_sw32_device(uint32_t rows, uint32_t cols, const uint32_t* row_offsets,
                                    const uint32_t* source_ids, const float* values, uint64_t nnz,
                                    int bucket_by_rw_mask, tcc_stream_t stream, tcc_sw32_device** out);
@@ -213,8 +216,10 @@ int tcc_sw32_device_arrays(const tcc_sw32_device* format, tcc_sw32_arrays* array
 /* The device view of all tasks, as an upload would give it (reference
  * src/device_matrix.cuh:8-37 builds the same view from its uploaded arrays). */
 int tcc_sw32_device_view_of(const tcc_sw32_device* format, tcc_sw32_device_view* view);
-/* Frees the arrays (synchronises the device). */
+/* Frees the arrays into the library's pool (synchronises the device). */
 void tcc_sw32_device_free(tcc_sw32_device* format);
+/* Returns the memory that the library's pool of the current device holds unused. */
+int tcc_sw32_device_trim(void);
 
 /* Multi-GPU sharding (no reference counterpart; the reference is single-GPU): cut the
  * task array into `parts` contiguous ranges at SW boundaries with balanced estimated cost

@@ -9,7 +9,8 @@ from .api import (BUCKET_ORDER, NO_PARTIAL, PADDING_SOURCE, TASK_PANEL_LIMIT, Cs
                   DeviceTimeout, InvalidArgument, MtxMatrix, SpmmWorkspace, Sw32DeviceFormat, Sw32HostFormat,
                   convert_csr_to_sw32, convert_csr_to_sw32_device, device_status, launch_spmm_int8,
                   load_matrix_market, make_canonical_csr, pack_features_int8x16, partition_tasks,
-                  quantize_features_int8, quantize_pack_features_int8, spmm_launch_shape, workspace_size)
+                  quantize_features_int8, quantize_pack_features_int8, spmm_launch_shape, sw32_device_trim,
+                  workspace_size)
 from ._native import library_path
 
 __all__ = [
@@ -17,5 +18,6 @@ __all__ = [
     "DeviceTimeout", "InvalidArgument", "MtxMatrix", "SpmmWorkspace", "Sw32DeviceFormat", "Sw32HostFormat",
     "convert_csr_to_sw32", "convert_csr_to_sw32_device", "device_status", "launch_spmm_int8", "load_matrix_market",
     "make_canonical_csr", "pack_features_int8x16", "partition_tasks", "quantize_features_int8",
-    "quantize_pack_features_int8", "spmm_launch_shape", "workspace_size", "library_path",
+    "quantize_pack_features_int8", "spmm_launch_shape", "sw32_device_trim", "workspace_size",
+    "library_path",
 ]

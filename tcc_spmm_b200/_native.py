@@ -116,6 +116,7 @@ SIGNATURES = {
     "tcc_sw32_device_arrays": (C.c_int, [C.c_void_p, C.POINTER(Sw32Arrays)]),
     "tcc_sw32_device_view_of": (C.c_int, [C.c_void_p, C.POINTER(Sw32DeviceView)]),
     "tcc_sw32_device_free": (None, [C.c_void_p]),
+    "tcc_sw32_device_trim": (C.c_int, []),
 }
 
 WL_SIGNATURES = {

@@ -463,6 +463,11 @@ def convert_csr_to_sw32_device(rows: int, cols: int, row_offsets, source_ids, va
         _handle=owner)
 
 
+def sw32_device_trim() -> None:
+    """Return the memory that the device format builder's pool (current device) holds unused."""
+    _check(N.lib().tcc_sw32_device_trim())
+
+
 def _np_of(torch_dtype):
     import torch
 

@@ -31,6 +31,7 @@
 
 #include <limits>
 #include <memory>
+#include <mutex>
 #include <vector>
 
 namespace tcc {
@@ -335,10 +336,36 @@ __global__ void fillTasksKernel(const u64* __restrict__ panelStart, const u32* _
     }
 }
 
-// Stream-ordered scratch, released (in stream order) when the build returns or throws.
+// The builder's device memory comes from a pool of this library, one per device, that keeps
+// what is freed into it (release threshold: unlimited), so that a later build maps no new
+// memory; tcc_sw32_device_trim() hands the unused part back to the device.
+constexpr int kMaxDevices = 64;
+std::mutex gPoolMutex;
+cudaMemPool_t gPools[kMaxDevices] = {};
+
+cudaMemPool_t builderPool(int device, bool create) {
+    if (device < 0 || device >= kMaxDevices)
+        throw CudaError("device ordinal out of range");
+    std::lock_guard<std::mutex> lock(gPoolMutex);
+    if (gPools[device] == nullptr && create) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        cudaMemPool_t pool = nullptr;
+        throwIf(cudaMemPoolCreate(&pool, &props));
+        u64 keep = ~u64(0);
+        throwIf(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        gPools[device] = pool;
+    }
+    return gPools[device];
+}
+
+// Stream-ordered scratch from the builder's pool, released in stream order when the build
+// returns or throws (or earlier, through release()).
 class Scratch {
   public:
-    explicit Scratch(cudaStream_t stream) : stream_(stream) {}
+    Scratch(cudaMemPool_t pool, cudaStream_t stream) : pool_(pool), stream_(stream) {}
     Scratch(const Scratch&) = delete;
     Scratch& operator=(const Scratch&) = delete;
     ~Scratch() {
@@ -347,13 +374,21 @@ class Scratch {
     }
     template <typename T> T* get(u64 count) {
         void* p = nullptr;
-        throwIf(cudaMallocAsync(&p, std::max<u64>(count * sizeof(T), 16), stream_));
+        throwIf(cudaMallocFromPoolAsync(&p, std::max<u64>(count * sizeof(T), 16), pool_, stream_));
         blocks_.push_back(p);
         return static_cast<T*>(p);
     }
     void* bytes(std::size_t n) { return get<unsigned char>(n); }
+    void release(void* p) {
+        auto it = std::find(blocks_.begin(), blocks_.end(), p);
+        if (it == blocks_.end())
+            return;
+        blocks_.erase(it);
+        throwIf(cudaFreeAsync(p, stream_));
+    }
 
   private:
+    cudaMemPool_t pool_;
     cudaStream_t stream_;
     std::vector<void*> blocks_;
 };
@@ -397,7 +432,8 @@ DeviceFormat buildOnDevice(u32 rows, u32 cols, const u32* offsets, const u32* so
         throw std::invalid_argument("invalid canonical CSR for source-mask SW32");
     DeviceFormat out(new tcc_sw32_device, tcc_sw32_device_free);
     throwIf(cudaGetDevice(&out->device));
-    Scratch scratch(stream);
+    cudaMemPool_t pool = builderPool(out->device, true);
+    Scratch scratch(pool, stream);
     BuildStatus* st = scratch.get<BuildStatus>(1);
     BuildStatus hs{};
     throwIf(cudaMemsetAsync(st, 0, sizeof(BuildStatus), stream));
@@ -438,13 +474,18 @@ DeviceFormat buildOnDevice(u32 rows, u32 cols, const u32* offsets, const u32* so
 
         cub::DoubleBuffer<u64> keyBuf(keyA, keyB);
         cub::DoubleBuffer<u32> posBuf(posA, posB);
+        // Only the window and source bits are sorted: the sort is stable and the entries come
+        // in CSR order, so an item's entries stay in increasing row order.
         const int endBit = static_cast<int>(winShift + windowBits);
         std::size_t tempBytes = 0;
-        throwIf(cub::DeviceRadixSort::SortPairs(nullptr, tempBytes, keyBuf, posBuf, n, 0, endBit, stream));
-        throwIf(cub::DeviceRadixSort::SortPairs(scratch.bytes(tempBytes), tempBytes, keyBuf, posBuf, n, 0, endBit,
-                                                stream));
+        throwIf(cub::DeviceRadixSort::SortPairs(nullptr, tempBytes, keyBuf, posBuf, n, 5, endBit, stream));
+        void* temp = scratch.bytes(tempBytes);
+        throwIf(cub::DeviceRadixSort::SortPairs(temp, tempBytes, keyBuf, posBuf, n, 5, endBit, stream));
         keys = keyBuf.Current();
         pos = posBuf.Current();
+        scratch.release(temp);
+        scratch.release(keyBuf.Alternate());
+        scratch.release(posBuf.Alternate());
 
         // 2. Items: first entry of every run of equal (window, source).
         heads = scratch.get<u32>(n);
@@ -477,10 +518,13 @@ DeviceFormat buildOnDevice(u32 rows, u32 cols, const u32* offsets, const u32* so
             const int endBit = static_cast<int>(4 + windowBits);
             std::size_t tempBytes = 0;
             throwIf(cub::DeviceRadixSort::SortPairs(nullptr, tempBytes, keyBuf, permBuf, items, 0, endBit, stream));
-            throwIf(cub::DeviceRadixSort::SortPairs(scratch.bytes(tempBytes), tempBytes, keyBuf, permBuf, items, 0,
-                                                    endBit, stream));
+            void* temp = scratch.bytes(tempBytes);
+            throwIf(cub::DeviceRadixSort::SortPairs(temp, tempBytes, keyBuf, permBuf, items, 0, endBit, stream));
             sortedKey = keyBuf.Current();
             perm = permBuf.Current();
+            scratch.release(temp);
+            scratch.release(keyBuf.Alternate());
+            scratch.release(permBuf.Alternate());
         }
         runsKernel<<<blocksFor(items), kThreads, 0, stream>>>(sortedKey, perm, itemMask, items, runStart, runEnd,
                                                              valueIndex);
@@ -543,7 +587,7 @@ DeviceFormat buildOnDevice(u32 rows, u32 cols, const u32* offsets, const u32* so
     z.partialIds = hs.parts;
     const u64 total = 256 * 9 + 4 * z.windowOffsets + 12 * z.sourceIds + 4 * z.rowGroupMasks + 4 * z.values +
                       4 * z.bucketOffsets + sizeof(tcc_sw32_task) * z.tasks + 8 * z.reductions + 4 * z.partialIds;
-    throwIf(cudaMalloc(&out->block, total));
+    throwIf(cudaMallocFromPoolAsync(&out->block, total, pool, stream));
     unsigned char* cursor = static_cast<unsigned char*>(out->block);
     u32* windowOffsets = carve<u32>(cursor, z.windowOffsets);
     u32* sourceIds = carve<u32>(cursor, z.sourceIds);
@@ -628,11 +672,24 @@ void tcc_sw32_device_free(tcc_sw32_device* format) {
         return;
     int current = 0;
     if (format->block != nullptr && cudaGetDevice(&current) == cudaSuccess) {
+        // Work on any stream may still read the arrays: wait for the device, then hand the
+        // block back to the builder's pool.
         cudaSetDevice(format->device);
-        cudaFree(format->block);
+        cudaDeviceSynchronize();
+        cudaFreeAsync(format->block, nullptr);
+        cudaStreamSynchronize(nullptr);
         cudaSetDevice(current);
     }
     delete format;
+}
+
+int tcc_sw32_device_trim(void) {
+    return tcc::guarded([&] {
+        int device = 0;
+        tcc::throwIf(cudaGetDevice(&device));
+        if (cudaMemPool_t pool = tcc::builderPool(device, false))
+            tcc::throwIf(cudaMemPoolTrimTo(pool, 0));
+    });
 }
 
 } // extern "C"
