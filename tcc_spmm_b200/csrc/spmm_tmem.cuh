@@ -125,12 +125,12 @@ __device__ __forceinline__ int tmemLaneFeature(int l) {
 
 // Consumer X step of chunk s: warp w gathers bytes 32w..32w+31 of the chunk's 32 packed source
 // rows (two 16-byte cp.async per row, invalid slots zero-filled) as one cp.async group, then
-// tells the producer that the chunk's IDs have been read. Returns false when the wait ran out.
-template <int F, int STAGES, int P>
+// (barUsed != 0) tells the producer that the chunk's IDs have been read. Returns false when the
+// wait ran out. L is the kernel's shared-memory layout.
+template <typename L, int F>
 __device__ __forceinline__ bool gatherSlice(unsigned char* smem, uint32_t xring, uint32_t barLand, uint32_t barUsed,
                                             const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
                                             uint32_t s, int lane, int w, uint64_t policy, bool ok) {
-    using L = Tmem<F, STAGES, P>;
     if (ok && s < total) {
         const uint32_t aslot = s % L::kARing;
         if (!boundedWait(barLand + 8 * aslot, (s / L::kARing) & 1)) {
@@ -150,7 +150,7 @@ __device__ __forceinline__ bool gatherSlice(unsigned char* smem, uint32_t xring,
                                    valid ? 16u : 0u, policy);
             }
             __syncwarp();
-            if (lane == 0)
+            if (lane == 0 && barUsed != 0)
                 dev::mbarArrive(barUsed + 8 * aslot);
         }
     }
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
         const uint32_t xLane = xring + 4 * g + 2 * c * L::kXRowStride;
         bool ok = true;
         for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
-            ok = gatherSlice<F, STAGES, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, polKeep, ok);
+            ok = gatherSlice<L, F>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, polKeep, ok);
         uint32_t seq = 0, windows = 0;
         tcc_sw32_task nextTask{};
         if (blockIdx.x < matrix.taskCount)
@@ -407,8 +407,8 @@ __global__ void __launch_bounds__(Tmem<F, STAGES, P>::kThreads, Tmem<F, STAGES, 
             const uint32_t panelCount = task.end - task.begin;
             const uint32_t nch = (panelCount + kChunk - 1) / kChunk;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
-                ok = gatherSlice<F, STAGES, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane,
-                                               warp, polKeep, ok);
+                ok = gatherSlice<L, F>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, warp,
+                                       polKeep, ok);
                 dev::cpAsyncWaitGroup<L::kPrefetch>();
                 __syncwarp();
                 // bFull[stage] also tells that the MMAs of chunk seq - kStages are complete
