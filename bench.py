@@ -52,6 +52,7 @@ def parse_args():
     p.add_argument("--e2e-slices", type=int, default=8, help="window-aligned task slices per end-to-end step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-gpu-format", action="store_true", help="skip timing the GPU SW32 construction")
+    p.add_argument("--no-assembly", action="store_true", help="skip the optional Y assembly across ranks")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
                             "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"],
@@ -298,6 +299,41 @@ def time_gpu_format(T, csr, fmt, device, repeats: int = 3) -> dict:
     return {"gpu_convert_ms": round(1e3 * sorted(times)[len(times) // 2], 2), "identical_to_host": identical}
 
 
+def time_assembly(fmt, bounds, y, F: int, rank: int, world: int, device, barrier, repeats: int = 5) -> dict:
+    """Optional assembly of the full Y on every rank (not part of the metric): one NCCL
+    broadcast per owner range, timed with CUDA events (max over ranks) after one untimed round,
+    and checked by per-range checksums against the owners' own rows."""
+    import torch
+    import torch.distributed as dist
+    from tcc_spmm_b200 import shards
+
+    ranges = shards.owned_rows(fmt, bounds)
+    shards.check_cover(ranges, fmt.rows)
+    lo, hi = ranges[rank]
+    own = torch.zeros(world, dtype=torch.float64, device=device)
+    own[rank] = y[lo:hi].double().sum() if hi > lo else 0.0
+    dist.all_reduce(own)
+    shards.assemble_rows(y, ranges)
+    torch.cuda.synchronize(device)
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(repeats):
+        shards.assemble_rows(y, ranges)
+    stop.record()
+    torch.cuda.synchronize(device)
+    ms = torch.tensor([start.elapsed_time(stop) / repeats], dtype=torch.float64, device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    seen = torch.stack([y[b:e].double().sum() if e > b else torch.zeros((), dtype=torch.float64, device=device)
+                        for b, e in ranges])
+    ok = torch.tensor([int(bool(torch.equal(seen, own)))], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    received = max(shards.received_bytes(ranges, r, F) for r in range(world))
+    t = float(ms.item())
+    return {"ms": round(t, 3), "bytes_received_per_rank_max": received, "gbs_per_rank": round(received / t / 1e6, 1),
+            "collective": "one NCCL broadcast per owner row range", "checksums_match": bool(ok.item())}
+
+
 def cpu_sample(fmt, features: int, target_seconds: float, threads: int, seed: int = 1):
     """Windows of a strided sample and their nnz, sized to about target_seconds of oracle work."""
     import oracle as O
@@ -444,6 +480,10 @@ def run_tcc(args):
                          f"oracle/tcc_oracle.c restatement of the reference arithmetic, {t:.2f} s",
                "seconds": round(t, 3), "threads_reported": O.max_threads()}
 
+    assembly = None
+    if world > 1 and not args.no_assembly:
+        assembly = time_assembly(fmt, bounds, y, F, rank, world, device, barrier)
+
     if not args.no_gpu_format:
         prep.update(time_gpu_format(T, csr, fmt, device))
 
@@ -470,6 +510,7 @@ def run_tcc(args):
                      "alg_bytes_per_launch": shard["total"], "compulsory_bytes": full["compulsory"],
                      "merge_bytes": full["merge_bytes"]},
         "clocks": clocks, "gpu_launches": args.steps, "e2e": e2e, "cpu_baseline": cpu,
+        "y_assembly": assembly,
     }
     print(json.dumps(line), flush=True)
 

@@ -1,0 +1,64 @@
+"""Task-range shards across ranks (one process per GPU) and the assembly of Y.
+
+The reference is single-GPU. Here the task array is cut into contiguous ranges at window
+boundaries (``partition_tasks``), so every split window, with its counter, partials and merge,
+lies inside one rank. A rank then writes exactly the Y rows of its windows: a contiguous range
+``[32 * first window, 32 * (last window + 1))`` (clipped to the matrix). The ranges of all
+ranks cover Y once.
+
+The assembly of the full Y on every rank is optional and is not part of the SpMM time: one
+broadcast per owner range over ``torch.distributed`` (NCCL over NVLink on GPUs, gloo on CPU),
+each straight into the owner's rows of every rank's Y, with no staging copy.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+
+def owned_rows(fmt, bounds: Sequence[int]) -> list:
+    """(row_begin, row_end) of Y owned by each rank, for the task bounds of partition_tasks."""
+    tasks = fmt.tasks
+    ranges = []
+    for r in range(len(bounds) - 1):
+        lo, hi = int(bounds[r]), int(bounds[r + 1])
+        if hi <= lo:
+            ranges.append((0, 0))
+            continue
+        first = 32 * int(tasks["sw"][lo])
+        last = min(fmt.rows, 32 * (int(tasks["sw"][hi - 1]) + 1))
+        ranges.append((first, last))
+    return ranges
+
+
+def check_cover(ranges: Sequence[tuple], rows: int) -> None:
+    """Raise ValueError unless the non-empty ranges tile [0, rows) in rank order."""
+    at = 0
+    for begin, end in ranges:
+        if end == begin:
+            continue
+        if begin != at or end < begin:
+            raise ValueError(f"row ranges do not tile Y: range [{begin}, {end}) after row {at}")
+        at = end
+    if at != rows:
+        raise ValueError(f"row ranges cover {at} of {rows} rows")
+
+
+def assemble_rows(y, ranges: Sequence[tuple], group=None) -> None:
+    """Give every rank the whole Y: rank r broadcasts its rows ranges[r] of y (a [rows, F]
+    row-major tensor on this rank's device) to all ranks, in rank order. Every rank must call
+    this with the same ranges (the collective order is the same on all ranks)."""
+    import torch.distributed as dist
+
+    if len(ranges) != dist.get_world_size(group):
+        raise ValueError("one row range per rank")
+    for r, (begin, end) in enumerate(ranges):
+        if end > begin:
+            dist.broadcast(y[begin:end], src=r, group=group)
+
+
+def received_bytes(ranges: Sequence[tuple], rank: int, features: int) -> int:
+    """Bytes of Y a rank receives in assemble_rows (every range but its own)."""
+    return int(sum(4 * features * (e - b) for r, (b, e) in enumerate(ranges) if r != rank))
+
+
+__all__ = ["owned_rows", "check_cover", "assemble_rows", "received_bytes"]
