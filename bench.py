@@ -300,8 +300,8 @@ def time_gpu_format(T, csr, fmt, device, repeats: int = 3) -> dict:
 
 
 def time_assembly(fmt, bounds, y, F: int, rank: int, world: int, device, barrier, repeats: int = 5) -> dict:
-    """Optional assembly of the full Y on every rank (not part of the metric): one NCCL
-    broadcast per owner range, timed with CUDA events (max over ranks) after one untimed round,
+    """Optional assembly of the full Y on every rank (not part of the metric): one broadcast
+    per owner range, all in one NCCL group, timed with CUDA events (max over ranks) after one untimed round,
     and checked by per-range checksums against the owners' own rows."""
     import torch
     import torch.distributed as dist
@@ -331,7 +331,8 @@ def time_assembly(fmt, bounds, y, F: int, rank: int, world: int, device, barrier
     received = max(shards.received_bytes(ranges, r, F) for r in range(world))
     t = float(ms.item())
     return {"ms": round(t, 3), "bytes_received_per_rank_max": received, "gbs_per_rank": round(received / t / 1e6, 1),
-            "collective": "one NCCL broadcast per owner row range", "checksums_match": bool(ok.item())}
+            "collective": "one broadcast per owner row range, all in one NCCL group",
+            "checksums_match": bool(ok.item())}
 
 
 def cpu_sample(fmt, features: int, target_seconds: float, threads: int, seed: int = 1):

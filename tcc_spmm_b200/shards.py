@@ -51,9 +51,17 @@ def assemble_rows(y, ranges: Sequence[tuple], group=None) -> None:
 
     if len(ranges) != dist.get_world_size(group):
         raise ValueError("one row range per rank")
-    for r, (begin, end) in enumerate(ranges):
-        if end > begin:
-            dist.broadcast(y[begin:end], src=r, group=group)
+    pieces = [(r, y[begin:end]) for r, (begin, end) in enumerate(ranges) if end > begin]
+    if y.is_cuda and dist.get_backend(group) == "nccl":
+        # One NCCL group: the owners' broadcasts run concurrently, so every link carries data
+        # in both directions at once.
+        with dist._coalescing_manager(group=group, device=y.device, async_ops=True) as cm:
+            for r, piece in pieces:
+                dist.broadcast(piece, src=r, group=group, async_op=True)
+        cm.wait()
+    else:
+        for r, piece in pieces:
+            dist.broadcast(piece, src=r, group=group)
 
 
 def received_bytes(ranges: Sequence[tuple], rank: int, features: int) -> int:
