@@ -53,6 +53,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-gpu-format", action="store_true", help="skip timing the GPU SW32 construction")
     p.add_argument("--no-assembly", action="store_true", help="skip the optional Y assembly across ranks")
+    p.add_argument("--natural-order", action="store_true",
+                   help="launch the tasks in format order instead of the balanced order (tcc_balance_tasks)")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
                             "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"],
@@ -410,7 +412,7 @@ def run_tcc(args):
     lo, hi = int(bounds[rank]), int(bounds[rank + 1])
     shard = shard_bytes(fmt, lo, hi, F)
     full = fmt.algorithmic_bytes(F)
-    dm = T.DeviceMatrix(fmt, F, device, task_range=(lo, hi))
+    dm = T.DeviceMatrix(fmt, F, device, task_range=(lo, hi), balance=not args.natural_order)
     x = W.normal_features(fmt.cols, F, threads=threads)
     xd = torch.from_numpy(x).to(device)
     packed = torch.empty(fmt.cols * F, dtype=torch.int8, device=device)
@@ -502,6 +504,7 @@ def run_tcc(args):
                    "tasks": int(fmt.tasks.size), "partial_count": fmt.partial_count,
                    "parallelism": f"task-range shards x{world}, X replicated, Y rows per rank",
                    "l2": "inputs larger than L2 (no flush)", "kernel": args.variant,
+                   "task_order": "format order" if args.natural_order else "balanced for the launch grid",
                    "launch": T.spmm_launch_shape(F, args.variant) if args.variant != "generic" else None,
                    "prep": prep},
         "hbm_gbs_alg": round(full["total"] / (ms_step / 1e3) / 1e9, 1),

@@ -230,6 +230,21 @@ int tcc_partition_tasks(const tcc_sw32_task* tasks, uint32_t task_count,
                         const uint32_t* row_group_masks, uint32_t features, uint32_t parts,
                         uint32_t* bounds);
 
+/* Task order for one launch (no reference counterpart; the reference launches one CTA per task):
+ * the fast-path kernels are persistent, CTA b of a grid of G = min(ctas, task_count) CTAs taking
+ * tasks b, b + G, b + 2G, ... of the view. out receives a permutation of tasks that deals them
+ * heaviest first (the cost estimate of tcc_partition_tasks), one per CTA per round, to the CTA
+ * with the least work so far, so that the CTAs finish together. Y is bit-identical for any task
+ * order. ctas = the grid of the launch (tcc_spmm_launch_shape); out must not alias tasks. */
+int tcc_balance_tasks(const tcc_sw32_task* tasks, uint32_t task_count, const uint32_t* row_group_masks,
+                      uint32_t features, uint32_t ctas, tcc_sw32_task* out);
+
+/* Launch shape of an SpMM kernel variant on the current device (variant 0 = what
+ * tcc_launch_spmm_int8 runs on 16-byte aligned arrays): grid (persistent CTAs; 0 for the
+ * per-task generic kernel), threads per CTA, dynamic shared memory and resident CTAs per SM. */
+int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32_t* threads, uint32_t* smem,
+                          int* occupancy);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -245,6 +245,18 @@ def partition_tasks(fmt: Sw32HostFormat, features: int, parts: int) -> np.ndarra
     return bounds
 
 
+def balance_tasks(tasks: np.ndarray, row_group_masks, features: int, ctas: int) -> np.ndarray:
+    """Task order for a persistent launch of `ctas` CTAs (CTA b takes tasks b, b + G, ...):
+    heaviest first, one per CTA per round, to the CTA with the least estimated work. A
+    permutation of `tasks`; Y does not depend on the order."""
+    src = np.ascontiguousarray(tasks)
+    out = np.empty_like(src)
+    masks = _u32(row_group_masks)
+    _check(N.lib().tcc_balance_tasks(src.ctypes.data_as(C.c_void_p), src.size, _ptr(masks, C.c_uint32), features,
+                                     ctas, out.ctypes.data_as(C.c_void_p)))
+    return out
+
+
 # --------------------------------------------------------------------------------------------
 # Device side (torch is used for device memory and streams only)
 # --------------------------------------------------------------------------------------------
@@ -278,9 +290,14 @@ class SpmmWorkspace:
 class DeviceMatrix:
     """Uploads every SW32 array and allocates the split-task workspace for `features`
     (reference src/device_matrix.cuh:8-37): partials = partialCount*8*F floats, counters =
-    windows*(F/128) zeroed u32 when partialCount > 0."""
+    windows*(F/128) zeroed u32 when partialCount > 0.
 
-    def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None):
+    balance=True also uploads the tasks in the order of balance_tasks for the grid of the
+    default kernel on this device; view() of the whole task range then uses that order
+    (sub-range views keep the natural order, whose ranges cover contiguous windows)."""
+
+    def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None,
+                 balance: bool = False):
         import torch
 
         self.rows, self.cols, self.features = fmt.rows, fmt.cols, features
@@ -300,6 +317,12 @@ class DeviceMatrix:
         tasks = fmt.tasks if task_range is None else fmt.tasks[task_range[0]:task_range[1]]
         self.task_count = int(tasks.size)
         self.tasks = up(np.ascontiguousarray(tasks).view(np.uint32), torch.int32)
+        self.tasks_balanced = None
+        if balance and self.task_count:
+            with torch.cuda.device(self.device):
+                grid = spmm_launch_shape(features)["grid"]
+            order = balance_tasks(tasks, fmt.row_group_masks, features, grid)
+            self.tasks_balanced = up(order.view(np.uint32), torch.int32)
         self.reductions = up(np.ascontiguousarray(fmt.reductions).view(np.uint32), torch.int32)
         self.partial_ids = up(fmt.partial_ids, torch.int32)
         self.partial_count = fmt.partial_count
@@ -315,10 +338,12 @@ class DeviceMatrix:
         last = self.task_count if last is None else last
         if not 0 <= first <= last <= self.task_count:
             raise ValueError("task range out of bounds")
+        whole = first == 0 and last == self.task_count
+        tasks = self.tasks_balanced if (whole and getattr(self, "tasks_balanced", None) is not None) else self.tasks
         return N.Sw32DeviceView(self.window_offsets.data_ptr(), self.source_ids.data_ptr(),
                                 self.row_group_masks.data_ptr(), self.source_metadata.data_ptr(),
                                 self.values.data_ptr(), self.bucket_offsets.data_ptr(),
-                                self.tasks.data_ptr() + TASK_DTYPE.itemsize * first, self.reductions.data_ptr(),
+                                tasks.data_ptr() + TASK_DTYPE.itemsize * first, self.reductions.data_ptr(),
                                 self.partial_ids.data_ptr(), last - first)
 
     @classmethod

@@ -16,6 +16,8 @@ CsrMatrix canonicalCsr(std::uint32_t rows, std::uint32_t cols, std::uint32_t nnz
 MtxMatrix loadMatrixMarketFile(const std::string& path);
 void partitionTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
                     std::uint32_t features, std::uint32_t parts, std::uint32_t* bounds);
+void balanceTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
+                  std::uint32_t features, std::uint32_t ctas, tcc_sw32_task* out);
 
 namespace {
 thread_local std::string lastError;
@@ -179,6 +181,15 @@ int tcc_partition_tasks(const tcc_sw32_task* tasks, uint32_t task_count, const u
         if (bounds == nullptr)
             throw std::invalid_argument("null bounds");
         tcc::partitionTasks(tasks, task_count, row_group_masks, features, parts, bounds);
+    });
+}
+
+int tcc_balance_tasks(const tcc_sw32_task* tasks, uint32_t task_count, const uint32_t* row_group_masks,
+                      uint32_t features, uint32_t ctas, tcc_sw32_task* out) {
+    return tcc::guarded([&] {
+        if (out == tasks && task_count != 0)
+            throw std::invalid_argument("out must not alias tasks");
+        tcc::balanceTasks(tasks, task_count, row_group_masks, features, ctas, out);
     });
 }
 

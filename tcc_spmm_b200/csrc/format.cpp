@@ -382,20 +382,23 @@ CsrMatrix canonicalCsr(std::uint32_t rows, std::uint32_t cols, std::uint32_t nnz
     return out;
 }
 
-// Balanced contiguous task ranges cut at window boundaries. Cost of a task: its panels
-// weighted by the row-group MMAs they issue, plus a fixed write-back term per task.
+// Estimated cost of a task: its panels weighted by the row-group MMAs they issue, plus a fixed
+// write-back term per task.
+double taskCost(const tcc_sw32_task& task, const std::uint32_t* masks, std::uint32_t features) {
+    double cost = 16.0 * (features / 128.0);
+    for (std::uint32_t p = task.begin; p < task.end; ++p)
+        cost += 8.0 + (masks ? 2.0 * __builtin_popcount(masks[p] & 15u) : 3.0);
+    return cost;
+}
+
+// Balanced contiguous task ranges cut at window boundaries.
 void partitionTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
                     std::uint32_t features, std::uint32_t parts, std::uint32_t* bounds) {
     if (parts == 0 || (count != 0 && tasks == nullptr))
         throw std::invalid_argument("invalid task partition request");
     std::vector<double> prefix(std::size_t(count) + 1, 0.0);
-    const double perTask = 16.0 * (features / 128.0);
-    for (std::uint32_t i = 0; i < count; ++i) {
-        double cost = perTask;
-        for (std::uint32_t p = tasks[i].begin; p < tasks[i].end; ++p)
-            cost += 8.0 + (masks ? 2.0 * __builtin_popcount(masks[p] & 15u) : 3.0);
-        prefix[i + 1] = prefix[i] + cost;
-    }
+    for (std::uint32_t i = 0; i < count; ++i)
+        prefix[i + 1] = prefix[i] + taskCost(tasks[i], masks, features);
     bounds[0] = 0;
     for (std::uint32_t k = 1; k < parts; ++k) {
         const double target = prefix[count] * k / parts;
@@ -408,6 +411,54 @@ void partitionTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::
         bounds[k] = std::max(cut, bounds[k - 1]);
     }
     bounds[parts] = count;
+}
+
+// Task order for a persistent launch of `ctas` CTAs in which CTA b takes tasks b, b + G, b + 2G,
+// ... (G = min(ctas, count)). The tasks are dealt heaviest first, in rounds of G: in each round
+// every CTA receives one task, the heaviest remaining going to the CTA with the least estimated
+// work so far, so the CTAs' task counts differ by at most one (the last, partial round goes to
+// the least-loaded CTAs, which take the lowest indices). The result is a permutation of the
+// input: the SpMM is independent of task order (every task writes only its own window's rows or
+// partial blocks, and the split-window merge sums partials in the reduce ranges' fixed order).
+void balanceTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
+                  std::uint32_t features, std::uint32_t ctas, tcc_sw32_task* out) {
+    if (ctas == 0 || (count != 0 && (tasks == nullptr || out == nullptr)))
+        throw std::invalid_argument("invalid task balance request");
+    if (count == 0)
+        return;
+    const std::uint32_t g = std::min(ctas, count);
+    std::vector<double> cost(count);
+    for (std::uint32_t i = 0; i < count; ++i)
+        cost[i] = taskCost(tasks[i], masks, features);
+    std::vector<std::uint32_t> order(count);
+    for (std::uint32_t i = 0; i < count; ++i)
+        order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](std::uint32_t a, std::uint32_t b) { return cost[a] > cost[b]; });
+    std::vector<std::vector<std::uint32_t>> bins(g);
+    std::vector<double> load(g, 0.0);
+    std::vector<std::uint32_t> byLoad(g);
+    for (std::uint32_t b = 0; b < g; ++b)
+        byLoad[b] = b;
+    for (std::uint32_t at = 0; at < count; at += g) {
+        const std::uint32_t n = std::min(g, count - at);
+        std::stable_sort(byLoad.begin(), byLoad.end(), [&](std::uint32_t a, std::uint32_t b) { return load[a] < load[b]; });
+        for (std::uint32_t i = 0; i < n; ++i) {
+            const std::uint32_t bin = byLoad[i], task = order[at + i];
+            bins[bin].push_back(task);
+            load[bin] += cost[task];
+        }
+    }
+    // CTAs b < count % g take one task more: put the bins that received one first.
+    const std::size_t full = count / g;
+    std::vector<std::uint32_t> binOrder(g);
+    for (std::uint32_t b = 0; b < g; ++b)
+        binOrder[b] = b;
+    std::stable_partition(binOrder.begin(), binOrder.end(), [&](std::uint32_t b) { return bins[b].size() > full; });
+    for (std::uint32_t b = 0; b < g; ++b) {
+        const auto& list = bins[binOrder[b]];
+        for (std::size_t k = 0; k < list.size(); ++k)
+            out[b + k * g] = tasks[list[k]];
+    }
 }
 
 } // namespace tcc

@@ -180,3 +180,22 @@ def test_matches_reference_kernel(tag, features):
     torch.cuda.synchronize()
     _, bound = oracle_y(case)
     assert_within_tf32_bound(y.cpu().numpy(), y_ref.cpu().numpy(), bound, f"reference {tag}")
+
+
+@pytest.mark.parametrize("features", [128, 256])
+@pytest.mark.parametrize("name", ["stress_small", "powerlaw_small"])
+def test_balanced_task_order_bit_identical(name, features):
+    """Y does not depend on the task order: the balanced order of tcc_balance_tasks gives the
+    same bits as the format order (split windows merge their partials in a fixed order)."""
+    torch = _torch()
+    case = build_case(W.generate(name), features, seed=17)
+    y = run_spmm(case)
+    balanced = T.DeviceMatrix(case.fmt, features, "cuda", balance=True)
+    assert balanced.tasks_balanced is not None
+    y2 = torch.full_like(y, float("nan"))
+    T.launch_spmm_int8(balanced.view(), case.packed_dev, case.scales_dev, y2, case.fmt.rows, case.fmt.cols,
+                       features, balanced.workspace())
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int32), y2.view(torch.int32))
+    assert int(balanced.counters.abs().sum()) == 0
+
