@@ -74,9 +74,9 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic(config: str, variant: str):
+def profile_traffic(config: str, variant: str, task_order: str):
     """ncu DRAM bytes of one launch of this config's kernel (profiles/traffic.json), when the
-    capture was taken of the same kernel variant."""
+    capture was taken of the same kernel variant and task order."""
     path = ROOT / "profiles" / "traffic.json"
     if not path.exists():
         return None
@@ -84,7 +84,9 @@ def profile_traffic(config: str, variant: str):
         entry = json.loads(path.read_text()).get(config)
     except Exception:
         return None
-    return entry if entry and entry.get("variant", "default") == variant else None
+    if not entry or entry.get("variant", "default") != variant or entry.get("task_order", "format") != task_order:
+        return None
+    return entry
 
 
 # ----------------------------------------------------------------------------------------
@@ -460,7 +462,8 @@ def run_tcc(args):
     peak, peak_kind = measured_peaks()
     launch_s = (ms_local / args.steps) / 1e3
     achieved = shard["total"] / launch_s / 1e9
-    traffic = profile_traffic(args.config, args.variant) if world == 1 else None
+    traffic = (profile_traffic(args.config, args.variant, "format" if args.natural_order else "balanced")
+               if world == 1 else None)
 
     # end to end through the public API with host buffers: every step copies packed X +
     # scales host -> device, runs the SpMM and copies this rank's Y rows device -> host. The
