@@ -57,7 +57,7 @@ def parse_args():
                    help="launch the tasks in format order instead of the balanced order (tcc_balance_tasks)")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
-                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"],
+                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4", "tmem8"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()
@@ -74,9 +74,10 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic(config: str, variant: str, task_order: str):
+def profile_traffic(config: str, variant: str, task_order: str, launch=None):
     """ncu DRAM bytes of one launch of this config's kernel (profiles/traffic.json), when the
-    capture was taken of the same kernel variant and task order."""
+    capture was taken of the same kernel variant, task order and launch shape (a changed kernel
+    behind the same variant name has another shape, and its old capture is not used)."""
     path = ROOT / "profiles" / "traffic.json"
     if not path.exists():
         return None
@@ -85,6 +86,9 @@ def profile_traffic(config: str, variant: str, task_order: str):
     except Exception:
         return None
     if not entry or entry.get("variant", "default") != variant or entry.get("task_order", "format") != task_order:
+        return None
+    if launch is not None and entry.get("launch") is not None and any(
+            entry["launch"].get(k) != launch.get(k) for k in ("grid", "threads", "smem")):
         return None
     return entry
 
@@ -464,7 +468,8 @@ def run_tcc(args):
     peak, peak_kind = measured_peaks()
     launch_s = (ms_local / args.steps) / 1e3
     achieved = shard["total"] / launch_s / 1e9
-    traffic = (profile_traffic(args.config, args.variant, "format" if args.natural_order else "balanced")
+    traffic = (profile_traffic(args.config, args.variant, "format" if args.natural_order else "balanced",
+                               T.spmm_launch_shape(F, args.variant) if args.variant != "generic" else None)
                if world == 1 else None)
 
     # end to end through the public API with host buffers: every step copies packed X +

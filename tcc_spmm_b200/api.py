@@ -500,7 +500,8 @@ def _np_of(torch_dtype):
 
 
 KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "persistent32x2": 4,
-                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7, "tmem2p1": 8, "tmem2p2": 9, "tmem4p2": 10, "tmem4p4": 11}
+                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7, "tmem2p1": 8, "tmem2p2": 9,
+                   "tmem4p2": 10, "tmem4p4": 11, "tmem8": 12}
 
 
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,

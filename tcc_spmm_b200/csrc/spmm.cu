@@ -8,10 +8,12 @@
 // [partialCount][8][F] of split tasks and the last-arriver merge with a wrapping
 // acquire-release ticket that returns every counter to zero.
 //
-// Three kernels:
-//   spmmTmemKernel (spmm_tmem.cuh): the fast path (tcgen05 MMAs, accumulators in tensor
-//     memory), used when packedX, Y, the partials, sourceIds and sourceMetadata are 16-byte
-//     aligned (always true for cudaMalloc'd buffers).
+// The kernels:
+//   spmmTmem8Kernel (spmm_tmem8.cuh): the fast path (tcgen05 MMAs, accumulators in tensor
+//     memory, 8-panel chunks), used when packedX, Y, the partials, sourceIds and
+//     sourceMetadata are 16-byte aligned (always true for cudaMalloc'd buffers).
+//   spmmTmemKernel (spmm_tmem.cuh): the same arithmetic with 4-panel chunks and two stages
+//     (variants 8-11).
 //   spmmPersistentKernel (spmm_persistent.cuh): mma.sync with register accumulators, when
 //     only the IDs or metadata are not 16-byte aligned.
 //   spmmGenericKernel (spmm_generic.cuh): any 2-byte aligned packedX (the reference's own
@@ -22,6 +24,7 @@
 #include "spmm_generic.cuh"
 #include "spmm_persistent.cuh"
 #include "spmm_tmem.cuh"
+#include "spmm_tmem8.cuh"
 
 #include <algorithm>
 #include <cuda_runtime.h>
@@ -31,7 +34,7 @@
 namespace tcc {
 namespace {
 
-constexpr int kDefaultVariant = 9; // spmmTmemKernel<F, 2, 2>
+constexpr int kDefaultVariant = 12; // spmmTmem8Kernel<F, 2>
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -82,14 +85,13 @@ struct LaunchShape {
     uint32_t grid = 0, smem = 0;
     int occupancy = 0; // resident CTAs per SM of this launch shape
 };
-template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
+template <typename L, auto Kernel> LaunchShape tmemShapeOf(int device) {
     static std::mutex mutex;
     static LaunchShape shape[64];
     std::lock_guard<std::mutex> lock(mutex);
     if (device < 0 || device >= 64)
         throw CudaError("device ordinal out of range");
     if (shape[device].grid == 0) {
-        using L = Tmem<F, STAGES, P>;
         int perSmBytes = 0, reserved = 0, optin = 0, sms = 0, regsPerSm = 0, threadsPerSm = 0;
         throwIf(cudaDeviceGetAttribute(&perSmBytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device));
         throwIf(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device));
@@ -101,10 +103,9 @@ template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
         const int bytes = (std::max(L::kBytes, floor) + 127) / 128 * 128;
         if (bytes > optin)
             throw CudaError("tensor-memory SpMM kernel does not fit on this device");
-        throwIf(cudaFuncSetAttribute(spmmTmemKernel<F, STAGES, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     bytes));
+        throwIf(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
         cudaFuncAttributes attr{};
-        throwIf(cudaFuncGetAttributes(&attr, spmmTmemKernel<F, STAGES, P>));
+        throwIf(cudaFuncGetAttributes(&attr, Kernel));
         // Registers are allocated per warp in units of 256 and each of the 4 SM sub-partitions
         // holds a quarter of the register file; the warps of the resident CTAs spread evenly.
         const int warps = L::kThreads / 32;
@@ -124,6 +125,24 @@ template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
     return shape[device];
 }
 
+template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
+    return tmemShapeOf<Tmem<F, STAGES, P>, spmmTmemKernel<F, STAGES, P>>(device);
+}
+template <int F, int P> LaunchShape tmem8Shape(int device) {
+    return tmemShapeOf<Tmem8<F, P>, spmmTmem8Kernel<F, P>>(device);
+}
+
+template <int F, int P>
+void launchTmem8(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
+                 uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
+    int device = 0;
+    throwIf(cudaGetDevice(&device));
+    const LaunchShape s = tmem8Shape<F, P>(device);
+    const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
+    spmmTmem8Kernel<F, P><<<grid, Tmem8<F, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols, partials,
+                                                                           counters);
+}
+
 template <int F, int STAGES, int P>
 void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
                 uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
@@ -138,13 +157,14 @@ void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* sca
 // variant: 0 = default fast path, 1 = generic kernel, 2/3 = persistent kernel with 32/64
 // features per consumer warp and one producer warp, 4/5 = the same with two producer warps,
 // 6/7 = with four producer warps, 8..11 = tensor-memory kernel with (stages, producer warps)
-// (2, 1), (2, 2), (4, 2), (4, 4).
+// (2, 1), (2, 2), (4, 2), (4, 4), 12 = tensor-memory kernel with 8-panel chunks, one stage and
+// two producer warps.
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
-    // Default: the tensor-memory kernel with two stages and two producer warps. It moves the
-    // IDs and metadata with bulk copies, which need 16-byte aligned arrays; otherwise the
+    // Default: the tensor-memory kernel with 8-panel chunks and two producer warps. It moves
+    // the IDs and metadata with bulk copies, which need 16-byte aligned arrays; otherwise the
     // persistent kernel runs.
     if (variant == 0)
         variant = kDefaultVariant;
@@ -171,8 +191,10 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
         launchTmem<F, 2, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else if (variant == 10) {
         launchTmem<F, 4, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else {
+    } else if (variant == 11) {
         launchTmem<F, 4, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else {
+        launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
     throwIf(cudaGetLastError());
 }
@@ -276,7 +298,7 @@ int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
     return tcc::guarded([&] {
-        if (variant < 0 || variant > 11)
+        if (variant < 0 || variant > 12)
             throw std::invalid_argument("unknown SpMM kernel variant");
         tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters,
                            reinterpret_cast<cudaStream_t>(stream), variant);
@@ -293,7 +315,7 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             throw std::invalid_argument("null output");
         if (features != 128 && features != 256)
             throw std::invalid_argument("feature dimension must be 128 or 256");
-        if (variant < 0 || variant > 11)
+        if (variant < 0 || variant > 12)
             throw std::invalid_argument("unknown SpMM kernel variant");
         int device = 0, sms = 1;
         tcc::throwIf(cudaGetDevice(&device));
@@ -324,6 +346,7 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             case 9: tmem(tcc::Tmem<128, 2, 2>{}, tcc::tmemShape<128, 2, 2>(device)); break;
             case 10: tmem(tcc::Tmem<128, 4, 2>{}, tcc::tmemShape<128, 4, 2>(device)); break;
             case 11: tmem(tcc::Tmem<128, 4, 4>{}, tcc::tmemShape<128, 4, 4>(device)); break;
+            case 12: tmem(tcc::Tmem8<128, 2>{}, tcc::tmem8Shape<128, 2>(device)); break;
             default: break;
             }
         } else {
@@ -334,6 +357,7 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             case 9: tmem(tcc::Tmem<256, 2, 2>{}, tcc::tmemShape<256, 2, 2>(device)); break;
             case 10: tmem(tcc::Tmem<256, 4, 2>{}, tcc::tmemShape<256, 4, 2>(device)); break;
             case 11: tmem(tcc::Tmem<256, 4, 4>{}, tcc::tmemShape<256, 4, 4>(device)); break;
+            case 12: tmem(tcc::Tmem8<256, 2>{}, tcc::tmem8Shape<256, 2>(device)); break;
             default: break;
             }
         }

@@ -93,7 +93,7 @@ __device__ __forceinline__ void namedBarrier(int id, int threads) {
 
 // Walks the chunks of this CTA's tasks (b, b+G, ...), skipping empty tasks. The next task's
 // panel range is prefetched when a task is entered.
-struct ChunkWalker {
+template <int CH> struct ChunkWalkerT {
     uint32_t slot, begin, end, next;
     uint32_t nBegin, nEnd;
     __device__ __forceinline__ void load(const tcc_sw32_device_view& m, uint32_t s, uint32_t& b, uint32_t& e) const {
@@ -125,18 +125,22 @@ struct ChunkWalker {
         enter(m);
     }
     __device__ __forceinline__ void advance(const tcc_sw32_device_view& m) {
-        next += kChunk;
+        next += CH;
         if (next >= end)
             enter(m);
     }
 };
 
-// Chunks of this CTA (computed by every warp).
-__device__ __forceinline__ uint32_t ctaChunkCount(const tcc_sw32_device_view& m, int lane) {
+// Chunks of CH panels of this CTA (computed by every warp).
+template <int CH> __device__ __forceinline__ uint32_t ctaChunkCountT(const tcc_sw32_device_view& m, int lane) {
     uint32_t total = 0;
     for (uint64_t t = blockIdx.x + uint64_t(lane) * gridDim.x; t < m.taskCount; t += 32ull * gridDim.x)
-        total += (m.tasks[t].end - m.tasks[t].begin + kChunk - 1) / kChunk;
+        total += (m.tasks[t].end - m.tasks[t].begin + CH - 1) / CH;
     return __reduce_add_sync(0xFFFFFFFFu, total);
+}
+using ChunkWalker = ChunkWalkerT<kChunk>;
+__device__ __forceinline__ uint32_t ctaChunkCount(const tcc_sw32_device_view& m, int lane) {
+    return ctaChunkCountT<kChunk>(m, lane);
 }
 
 // Consumer X step: gather warp c's FPW-byte slice of the 32 source rows of chunk s into its X

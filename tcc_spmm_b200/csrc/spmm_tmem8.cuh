@@ -1,0 +1,519 @@
+// Tensor-memory SpMM kernel with 8-panel chunks and one tensor-memory stage (tcgen05, sm_100a).
+//
+// Same arithmetic, roles and hand-offs as spmm_tmem.cuh (see there): per panel and 128-feature
+// slice one tcgen05.mma.kind::tf32 D[128 x 64] += A[128 x 8] * B[8 x 64], A the exact INT8
+// feature values in tensor memory, B the panel's values times the source scales as a TF32
+// hi/lo pair, D the window's accumulator, Y row j = D[:, j] + D[:, 32 + j].
+//
+// What differs is the unit of the pipeline. A chunk here is 8 panels (64 source slots) instead
+// of 4, so every per-chunk cost of the pipeline (waits and arrivals, ring bookkeeping, the ID,
+// metadata, scale and value staging, the loop) is paid once per 8 panels. In spmm_tmem.cuh those
+// costs are about two thirds of the instructions. Tensor memory holds one A stage of 64 columns
+// and the 64-column accumulator (128 columns, 4 CTAs per SM at F = 128), and shared memory one
+// buffer of B tiles, so the stage is refilled only after the MMAs of chunk c are complete. The
+// producer (B tiles) and the consumers (A columns) then refill it at the same time, both
+// waiting on that commit, and the MMA thread waits for both. The other CTAs of the SM fill the
+// gap. Power-law F128: 6.53 ms against 7.47 for spmm_tmem.cuh. With the consumers instead
+// chained behind the producer's B build, as in spmm_tmem.cuh, this kernel took 7.55 ms.
+//
+// Roles (chunks of the CTA's tasks b, b+G, ... form one stream; producer pw owns chunks pw,
+// pw+P, ...):
+//   consumers 0..F/32-1  warp w owns TMEM lane quarter w%4 of slice w/4 (32 features). X step
+//                        (kPrefetch chunks ahead): cp.async of its 32 bytes of the chunk's 64
+//                        source rows into a 32-byte-stride ring; within each panel row r is
+//                        stored at position r/2 + 4(r%2), so the two rows a lane reads (2c and
+//                        2c + 1) of all lanes fall in different banks. Then the A columns.
+//   producers (P warps)  A step (bulk copies of the chunk's 64 IDs and metadata words), V step
+//                        (cp.async of the value range and 64 scales; each lane two slots), B
+//                        step (the chunk's 8 B tiles in the one shared-memory B buffer).
+//   MMA warp             one thread issues the chunk's MMAs and the commits.
+// Synchronisation: bFull (producer -> MMA: B tiles written), aFull (consumers -> MMA: A columns
+// stored), sFree[c % 2] (MMA commit of chunk c -> the producer and the consumers of chunk c + 1,
+// who then refill the B tiles and the A columns at the same time), dFull/dFree for the
+// accumulator, aLand/aUsed and vFull for the producer rings. All waits bounded.
+#pragma once
+#include "spmm_tmem.cuh"
+
+namespace tcc {
+namespace {
+
+constexpr int kChunk8 = 8; // panels per chunk: 64 source slots, two per producer lane
+
+template <int F, int P> struct Tmem8 {
+    static constexpr int kSlices = F / 128;
+    static constexpr int kConsumers = F / 32;
+    static constexpr int kProducers = P;
+    static constexpr int kProducerWarp = kConsumers;
+    static constexpr int kMmaWarp = kConsumers + P;
+    static constexpr int kThreads = 32 * (kConsumers + P + 1);
+    static constexpr int kSlots = 8 * kChunk8;
+    // Consumer X rings (one per consumer warp): 64 rows x 32 bytes per chunk.
+    static constexpr int kXDepth = 3;
+    static constexpr int kPrefetch = kXDepth - 1;
+    static constexpr int kXSlotBytes = kSlots * 32;
+    // Producer rings.
+    static constexpr int kALead = 5, kARing = 8;
+    static constexpr int kVLead = 3, kVRing = 4;
+    static constexpr int kVCap = 256;
+    static constexpr int kHeaderOff = 4 * kSlots + 8 * kSlots;  // after ids and metadata
+    static constexpr int kASlotBytes = kHeaderOff + 16;
+    static constexpr int kVSlotBytes = kVCap * 4 + 4 * kSlots; // values, scales
+    static constexpr int kBTileBytes = 2048;
+    static constexpr int kBOff = 0;
+    static constexpr int kXOff = kBOff + kChunk8 * kBTileBytes;
+    static constexpr int kAOff = kXOff + kConsumers * kXDepth * kXSlotBytes;
+    static constexpr int kVOff = kAOff + kARing * kASlotBytes;
+    static constexpr int kVBaseOff = kVOff + kVRing * kVSlotBytes;
+    static constexpr int kFlagOff = kVBaseOff + 32;
+    static constexpr int kBarOff = kFlagOff + 16;
+    // bFull, aFull, sFree [2] (by chunk parity); dFull, dFree (two words reserved each); aLand,
+    // aUsed [kARing]; vFull [kVRing]; drain
+    static constexpr int kBars = 4 + 4 + 2 * kARing + kVRing + 1;
+    static constexpr int kBytes = kBarOff + 8 * kBars;
+    // Tensor memory per slice: the A stage (64 columns: 8 panels x 8 sources) and the
+    // accumulator (64 columns).
+    static constexpr int kSliceCols = 8 * kChunk8 + 64;
+    static constexpr int kColsUsed = kSlices * kSliceCols;
+    static constexpr int kTmemCols = kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
+    static constexpr int kMaxCtasPerSm = 512 / kTmemCols;
+    static_assert(kColsUsed <= 512, "tensor memory");
+    static_assert(kVRing <= 8 && kARing >= kALead + 2 && kVRing > kVLead && kALead > kVLead && kPrefetch <= kALead,
+                  "rings");
+    static_assert(kARing % P == 0 && kVRing % P == 0, "every ring slot has one producer");
+    static_assert(P == 1 || P == 2, "sFree[c % 2] gives each producer consecutive phases only for P <= 2");
+    static_assert(kASlotBytes % 16 == 0 && kXOff % 16 == 0 && kAOff % 16 == 0 && kVOff % 16 == 0 && kBarOff % 8 == 0,
+                  "alignment");
+    static constexpr uint32_t kIdesc = Tmem<F, 2, 2>::kIdesc;
+};
+
+// Position of row r (0..63) of a chunk in the consumer's X slot: within each panel (8 rows) the
+// even rows come first, so rows 2c and 2c + 1 of the four lane groups c hit distinct banks.
+__device__ __forceinline__ uint32_t xRowSlot(uint32_t row) {
+    return (row & ~7u) + ((row & 7u) >> 1) + 4 * (row & 1u);
+}
+
+// Consumer X step of chunk s: warp w gathers bytes 32w..32w+31 of the chunk's 64 packed source
+// rows (two 16-byte cp.async per row, invalid slots zero-filled) as one cp.async group, then
+// tells the producer that the chunk's IDs have been read. Returns false when the wait ran out.
+template <int F, int P>
+__device__ __forceinline__ bool gatherSlice8(unsigned char* smem, uint32_t xring, uint32_t barLand, uint32_t barUsed,
+                                             const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
+                                             uint32_t s, int lane, int w, uint64_t policy, bool ok) {
+    using L = Tmem8<F, P>;
+    if (ok && s < total) {
+        const uint32_t aslot = s % L::kARing;
+        if (!boundedWait(barLand + 8 * aslot, (s / L::kARing) & 1)) {
+            ok = false;
+        } else {
+            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+            const uint32_t dst = xring + (s % L::kXDepth) * L::kXSlotBytes;
+#pragma unroll
+            for (int pass = 0; pass < 4; ++pass) {
+                const uint32_t row = pass * 16 + (lane >> 1), piece = lane & 1;
+                const uint32_t id = (row >> 3) < np ? reinterpret_cast<const uint32_t*>(a)[row] : 0xFFFFFFFFu;
+                const bool valid = id < cols;
+                dev::cpAsync16Hint(dst + xRowSlot(row) * 32 + 16 * piece,
+                                   valid ? static_cast<const void*>(packedX + uint64_t(id) * F + 32 * w + 16 * piece)
+                                         : static_cast<const void*>(packedX),
+                                   valid ? 16u : 0u, policy);
+            }
+            __syncwarp();
+            if (lane == 0)
+                dev::mbarArrive(barUsed + 8 * aslot);
+        }
+    }
+    dev::cpAsyncCommit();
+    return ok;
+}
+
+template <int F, int P>
+__global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPerSm)
+    spmmTmem8Kernel(const tcc_sw32_device_view matrix, const int8_t* __restrict__ packedX,
+                    const float* __restrict__ scales, float* __restrict__ output, uint32_t rows, uint32_t cols,
+                    float* __restrict__ partials, uint32_t* __restrict__ counters) {
+    using L = Tmem8<F, P>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = dev::smemAddr(smem);
+    const uint32_t barB = base + L::kBarOff;   // bFull
+    const uint32_t barA = barB + 8;            // aFull
+    const uint32_t barS = barA + 8;            // sFree [2]
+    const uint32_t barD = barS + 16;           // dFull [2]
+    const uint32_t barR = barD + 16;           // dFree [2]
+    const uint32_t barL = barR + 16;           // aLand [kARing]
+    const uint32_t barU = barL + 8 * L::kARing; // aUsed [kARing]
+    const uint32_t barV = barU + 8 * L::kARing; // vFull [kVRing]
+    const uint32_t barF = barV + 8 * L::kVRing; // drain
+    volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(smem + L::kFlagOff);
+    if (threadIdx.x == 0) {
+        dev::mbarInit(barB, 1);
+        dev::mbarInit(barA, L::kConsumers);
+        dev::mbarInit(barS, 1);
+        dev::mbarInit(barS + 8, 1);
+        for (int d = 0; d < 2; ++d) {
+            dev::mbarInit(barD + 8 * d, 1);
+            dev::mbarInit(barR + 8 * d, L::kConsumers);
+        }
+        for (int s = 0; s < L::kARing; ++s) {
+            dev::mbarInit(barL + 8 * s, 1);
+            dev::mbarInit(barU + 8 * s, L::kConsumers);
+        }
+        for (int s = 0; s < L::kVRing; ++s)
+            dev::mbarInit(barV + 8 * s, 32);
+        dev::mbarInit(barF, 1);
+        flags[0] = flags[1] = flags[3] = 0; // flags[2] receives the TMEM address (allocating warp)
+        dev::fenceBarrierInit();
+    }
+    if (warp == L::kMmaWarp) {
+        dev::tmemAlloc(base + L::kFlagOff + 8, L::kTmemCols);
+        dev::tmemRelinquish();
+    }
+    dev::tcFenceBefore();
+    __syncthreads();
+    dev::tcFenceAfter();
+    const uint32_t tmem = flags[2];
+    const uint32_t total = ctaChunkCountT<kChunk8>(matrix, lane);
+
+    if (warp >= L::kProducerWarp && warp < L::kMmaWarp) {
+        // =================================== producers ====================================
+        const uint64_t polStream = dev::policyEvictFirst();
+        const uint64_t polKeep = dev::policyEvictLast();
+        uint32_t* vBase = reinterpret_cast<uint32_t*>(smem + L::kVBaseOff);
+        const uint32_t pw = warp - L::kProducerWarp;
+        ChunkWalkerT<kChunk8> walk;
+        walk.start(matrix);
+        for (uint32_t i = 0; i < pw; ++i)
+            walk.advance(matrix);
+        uint32_t seqA = pw, seqV = pw;
+        bool ok = true;
+        for (uint32_t seqF = pw; seqF < total && ok; seqF += P) {
+            // ---- A steps: IDs and metadata of chunks up to seqF + kALead (one lane) ----
+            for (; seqA < total && seqA <= seqF + L::kALead; seqA += P) {
+                const uint32_t slot = seqA % L::kARing;
+                if (seqA >= uint32_t(L::kARing) && !boundedWait(barU + 8 * slot, ((seqA / L::kARing) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t p0 = walk.next;
+                const uint32_t np = min(uint32_t(kChunk8), walk.end - p0);
+                if (lane == 0) {
+                    const uint32_t a = base + L::kAOff + slot * L::kASlotBytes;
+                    uint32_t* header =
+                        reinterpret_cast<uint32_t*>(smem + L::kAOff + slot * L::kASlotBytes + L::kHeaderOff);
+                    header[0] = p0;
+                    header[1] = np;
+                    dev::fenceProxyAsyncShared(); // earlier generic reads of the slot before the copies
+                    dev::mbarArriveExpectTx(barL + 8 * slot, 96 * np);
+                    dev::bulkCopyG2SHint(a, matrix.sourceIds + uint64_t(p0) * 8, 32 * np, barL + 8 * slot, polStream);
+                    dev::bulkCopyG2SHint(a + 4 * L::kSlots, matrix.sourceMetadata + uint64_t(p0) * 8, 64 * np,
+                                         barL + 8 * slot, polStream);
+                }
+#pragma unroll
+                for (int i = 0; i < P; ++i)
+                    walk.advance(matrix);
+            }
+            if (!ok)
+                break;
+            __syncwarp();
+            // ---- V steps: value ranges and scales of chunks up to seqF + kVLead ----
+            for (; seqV < seqA && seqV <= seqF + L::kVLead; seqV += P) {
+                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing;
+                if (!boundedWait(barL + 8 * aslot, (seqV / L::kARing) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+                unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
+                const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+                uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t slot = lane + 32 * h;
+                    const bool inRange = (slot >> 3) < np;
+                    const uint32_t id = inRange ? reinterpret_cast<const uint32_t*>(a)[slot] : 0xFFFFFFFFu;
+                    const uint64_t meta =
+                        inRange ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
+                    const bool valid = id < cols;
+                    dev::cpAsync4Hint(dev::smemAddr(v + 4 * L::kVCap + 4 * slot),
+                                      valid ? static_cast<const void*>(scales + id) : static_cast<const void*>(scales),
+                                      valid ? 4u : 0u, polKeep);
+                    const uint32_t mask = static_cast<uint32_t>(meta);
+                    const uint32_t first = static_cast<uint32_t>(meta >> 32);
+                    if (mask) {
+                        lo = min(lo, first);
+                        hi = max(hi, first + __popc(mask));
+                    }
+                }
+                lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+                hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+                const uint32_t count = hi > lo ? hi - lo : 0u;
+                if (lane == 0)
+                    vBase[vslot] = count <= uint32_t(L::kVCap) ? lo : 0xFFFFFFFFu;
+                if (count <= uint32_t(L::kVCap))
+                    for (uint32_t i = lane; i < count; i += 32)
+                        dev::cpAsync4Hint(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4, polStream);
+                dev::cpAsyncArriveNoinc(barV + 8 * vslot);
+            }
+            if (!ok)
+                break;
+            // ---- B step: the B tiles of chunk seqF, once the MMAs of chunk seqF - 1 are done.
+            // Chunk c's commit goes to sFree[c % 2], so each producer waits on consecutive
+            // phases of one barrier (the parity of a phase two ahead would be ambiguous). ----
+            const uint32_t aslot = seqF % L::kARing, vslot = seqF % L::kVRing;
+            if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1) ||
+                (seqF >= 1 && !boundedWaitBackoff(barS + 8 * ((seqF - 1) & 1), ((seqF - 1) >> 1) & 1))) {
+                ok = false;
+                break;
+            }
+            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
+            const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+            unsigned char* tiles = smem + L::kBOff;
+            {
+                uint4* z = reinterpret_cast<uint4*>(tiles);
+#pragma unroll
+                for (int i = 0; i < kChunk8 * L::kBTileBytes / 16 / 32; ++i)
+                    z[i * 32 + lane] = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+            const uint32_t vb = vBase[vslot];
+            const float* vsm = reinterpret_cast<const float*>(v);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t slot = lane + 32 * h;
+                const uint32_t pp = slot >> 3, k = slot & 7;
+                const uint64_t meta = pp < np ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
+                const float scale = reinterpret_cast<const float*>(v + 4 * L::kVCap)[slot];
+                uint32_t mask = static_cast<uint32_t>(meta);
+                const uint32_t first = static_cast<uint32_t>(meta >> 32);
+                uint32_t* tile = reinterpret_cast<uint32_t*>(tiles + pp * L::kBTileBytes + (k >> 2) * 128 + (k & 3) * 4);
+                uint32_t j = 0;
+                while (mask) {
+                    const int r = __ffs(mask) - 1;
+                    mask &= mask - 1;
+                    const float value = vb != 0xFFFFFFFFu ? vsm[first + j - vb] : __ldg(matrix.values + first + j);
+                    ++j;
+                    const float b = __uint_as_float(dev::tf32Exact(value)) * scale;
+                    const uint32_t bh = dev::tf32Exact(b);
+                    const uint32_t bl = dev::tf32Exact(b - __uint_as_float(bh));
+                    tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = bh;
+                    tile[((r & 7) * 16 + (r >> 3) * 256 + 1024) / 4] = bl;
+                }
+            }
+            dev::fenceProxyAsyncShared();
+            __syncwarp();
+            if (lane == 0)
+                dev::mbarArrive(barB);
+        }
+        if (!ok)
+            flags[1] = 1;
+        dev::cpAsyncWaitAll();
+        // No bulk copy may still be writing into this CTA's shared memory at exit.
+        for (uint32_t s = seqA >= L::kARing + pw ? seqA - L::kARing : pw; s < seqA; s += P)
+            boundedWait(barL + 8 * (s % L::kARing), (s / L::kARing) & 1);
+    } else if (warp == L::kMmaWarp) {
+        // ================================ MMA issuer (one thread) =========================
+        if (lane == 0) {
+            bool ok = true, issued = false;
+            uint32_t seq = 0, windows = 0;
+            for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
+                const tcc_sw32_task task = matrix.tasks[tk];
+                const uint32_t panelCount = task.end - task.begin;
+                if (panelCount == 0)
+                    continue;
+                if (ok && windows >= 1 && !boundedWaitBackoff(barR, (windows - 1) & 1))
+                    ok = false;
+                ++windows;
+                dev::tcFenceAfter();
+                const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
+                for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                    if (ok && (!boundedWaitBackoff(barA, seq & 1) || !boundedWaitBackoff(barB, seq & 1)))
+                        ok = false;
+                    if (!ok)
+                        continue;
+                    dev::tcFenceAfter();
+                    const uint32_t inChunk = min(uint32_t(kChunk8), panelCount - ch * kChunk8);
+                    for (uint32_t pp = 0; pp < inChunk; ++pp) {
+                        const unsigned long long desc = bTileDesc(base + L::kBOff + pp * L::kBTileBytes);
+#pragma unroll
+                        for (int sl = 0; sl < L::kSlices; ++sl)
+                            dev::mmaTf32Ts(tmem + sl * L::kSliceCols + 8 * kChunk8, tmem + sl * L::kSliceCols + 8 * pp,
+                                           desc, L::kIdesc, (ch | pp) != 0);
+                    }
+                    issued = true;
+                    dev::tcCommit(barS + 8 * (seq & 1));
+                }
+                if (ok)
+                    dev::tcCommit(barD);
+            }
+            if (issued) { // every MMA is complete before the tensor memory is released
+                dev::tcCommit(barF);
+                if (!boundedWait(barF, 0))
+                    ok = false;
+            }
+            if (!ok)
+                flags[1] = 1;
+        }
+        __syncwarp();
+    } else {
+        // ==================================== consumers ===================================
+        const int quarter = warp & 3, slice = warp >> 2;
+        const int g = lane >> 2, c = lane & 3;
+        const uint64_t polKeep = dev::policyEvictLast();
+        const uint32_t xring = base + L::kXOff + warp * L::kXDepth * L::kXSlotBytes;
+        const uint32_t tLane = uint32_t(32 * quarter) << 16;
+        const uint32_t aTmem = tmem + slice * L::kSliceCols + tLane;
+        const uint32_t dTmem = tmem + slice * L::kSliceCols + 8 * kChunk8 + tLane;
+        const uint32_t feature = slice * 128 + 32 * quarter + tmemLaneFeature(lane);
+        // Rows 2c and 2c + 1 of panel pp sit at positions 8pp + c and 8pp + 4 + c.
+        const uint32_t xLane = xring + 4 * g + 32 * c;
+        bool ok = true;
+        for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
+            ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, polKeep, ok);
+        uint32_t seq = 0, windows = 0;
+        tcc_sw32_task nextTask{};
+        if (blockIdx.x < matrix.taskCount)
+            nextTask = matrix.tasks[blockIdx.x];
+        for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
+            const tcc_sw32_task task = nextTask;
+            if (tk + gridDim.x < matrix.taskCount)
+                nextTask = matrix.tasks[tk + gridDim.x];
+            const uint32_t panelCount = task.end - task.begin;
+            const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
+            for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, warp,
+                                        polKeep, ok);
+                dev::cpAsyncWaitGroup<L::kPrefetch>();
+                __syncwarp();
+                // The MMAs of chunk seq - 1 are complete: the A columns may be rewritten (the
+                // producer refills the B tiles at the same time).
+                if (ok && seq >= 1 && !boundedWait(barS + 8 * ((seq - 1) & 1), ((seq - 1) >> 1) & 1))
+                    ok = false;
+                if (!ok)
+                    continue;
+                dev::tcFenceAfter();
+                const uint32_t xs = xLane + (seq % L::kXDepth) * L::kXSlotBytes;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t lo[16], hi[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int pp = 4 * half + q;
+                        const uint32_t wa = dev::ldsU32(xs + 256 * pp) ^ 0x80808080u;
+                        const uint32_t wb = dev::ldsU32(xs + 256 * pp + 128) ^ 0x80808080u;
+                        dev::int8PairToFloat<0>(wa, wb, lo[4 * q + 0], lo[4 * q + 1]);
+                        dev::int8PairToFloat<1>(wa, wb, lo[4 * q + 2], lo[4 * q + 3]);
+                        dev::int8PairToFloat<2>(wa, wb, hi[4 * q + 0], hi[4 * q + 1]);
+                        dev::int8PairToFloat<3>(wa, wb, hi[4 * q + 2], hi[4 * q + 3]);
+                    }
+                    dev::tcStore16x256bx4(aTmem + 32 * half, lo);
+                    dev::tcStore16x256bx4(aTmem + 32 * half + (16u << 16), hi);
+                }
+                dev::tcWaitSt();
+                dev::tcFenceBefore();
+                __syncwarp();
+                if (lane == 0)
+                    dev::mbarArrive(barA);
+            }
+            // ---- epilogue of this window ----
+            const uint32_t rowBase = task.sw * 32;
+            const bool split = task.partial != kNoPartial;
+            const bool haveWs = !split || (partials != nullptr && counters != nullptr);
+            if (!haveWs && threadIdx.x == 0)
+                atomicOr(&gDeviceStatus, 2u);
+            bool loaded = false;
+            if (panelCount > 0) {
+                if (ok && !boundedWait(barD, windows & 1))
+                    ok = false;
+                ++windows;
+                loaded = ok;
+                if (loaded)
+                    dev::tcFenceAfter();
+            }
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t h[16], l[16];
+                if (loaded) {
+                    dev::tcLoad32x32bx16(dTmem + 16 * half, h);
+                    dev::tcLoad32x32bx16(dTmem + 32 + 16 * half, l);
+                    dev::tcWaitLd();
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        h[j] = l[j] = 0u;
+                }
+                if (!haveWs)
+                    continue;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int row = 16 * half + j;
+                    const float y = __uint_as_float(h[j]) + __uint_as_float(l[j]);
+                    if (!split) {
+                        if (rowBase + row < rows)
+                            __stcs(output + uint64_t(rowBase + row) * F + feature, y);
+                    } else if (task.mask & (1u << (row >> 3))) {
+                        const uint64_t block = task.partial + __popc(task.mask & ((1u << (row >> 3)) - 1));
+                        __stcg(partials + (block * 8 + (row & 7)) * F + feature, y);
+                    }
+                }
+            }
+            if (panelCount > 0) {
+                if (loaded)
+                    dev::tcFenceBefore();
+                __syncwarp();
+                if (lane == 0)
+                    dev::mbarArrive(barR);
+            }
+            if (!split || !haveWs)
+                continue;
+            // Last-arriver merge among the consumer warps (reference src/kernel/spmm_kernel.cuh:250-282).
+            __threadfence();
+            namedBarrier(1, 32 * L::kConsumers);
+            if (threadIdx.x == 0 && ok) {
+                const uint32_t ticket =
+                    dev::ticketIncrement(counters + uint64_t(task.sw) * (F / 128), task.chunks - 1);
+                flags[0] = ticket == task.chunks - 1 ? 1u : 0u;
+            }
+            namedBarrier(1, 32 * L::kConsumers);
+            const bool last = ok && flags[0] != 0;
+            if (last) {
+                __threadfence();
+                constexpr uint32_t kVec = F / 4;
+                for (uint32_t rw = 0; rw < 4; ++rw) {
+                    const uint32_t row0 = rowBase + 8 * rw;
+                    if (row0 >= rows)
+                        break;
+                    const tcc_sw32_reduce_range red = matrix.reductions[task.reduceFirst + rw];
+                    const uint32_t validRows = min(8u, rows - row0);
+                    for (uint32_t e = threadIdx.x; e < validRows * kVec; e += 32 * L::kConsumers) {
+                        const uint32_t r = e / kVec, vv = e % kVec;
+                        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (uint32_t item = red.begin; item < red.end; ++item) {
+                            const uint64_t blk = matrix.partialIds[item];
+                            const float4 p = __ldcg(reinterpret_cast<const float4*>(partials + (blk * 8 + r) * F) + vv);
+                            sum.x += p.x;
+                            sum.y += p.y;
+                            sum.z += p.z;
+                            sum.w += p.w;
+                        }
+                        __stcs(reinterpret_cast<float4*>(output + uint64_t(row0 + r) * F) + vv, sum);
+                    }
+                }
+            }
+            namedBarrier(1, 32 * L::kConsumers); // flags[0] is reused by the next split task
+        }
+        dev::cpAsyncWaitAll();
+        if (!ok)
+            flags[1] = 1;
+    }
+    dev::tcFenceBefore();
+    __syncthreads();
+    dev::tcFenceAfter();
+    if (warp == L::kMmaWarp)
+        dev::tmemDealloc(tmem, L::kTmemCols);
+}
+
+} // namespace
+} // namespace tcc

@@ -22,7 +22,8 @@ def _torch():
     return torch
 
 
-@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"])
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64", "tmem2p1", "tmem2p2",
+                                     "tmem4p2", "tmem4p4", "tmem8"])
 @pytest.mark.parametrize("features", [128, 256])
 @pytest.mark.parametrize("name", sorted(EDGE_CASES))
 def test_edge_cases_within_tf32_bound(name, features, variant):
@@ -63,7 +64,7 @@ def test_single_term_rows_bit_exact(variant):
 
 
 @pytest.mark.parametrize("features", [128, 256])
-@pytest.mark.parametrize("variant", ["default", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4"])
+@pytest.mark.parametrize("variant", ["default", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4", "tmem8"])
 def test_single_term_rows_within_half_bound(variant, features):
     """The tensor-memory kernel folds the scale into the values (q * (tf32(a) * s) to 22 bits):
     a single term is within 2^-11 relative of the reference's tf32_rna(a) * tf32_rna(q*s), half
