@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             // phases of one barrier (the parity of a phase two ahead would be ambiguous). ----
             const uint32_t aslot = seqF % L::kARing, vslot = seqF % L::kVRing;
             if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1) ||
-                (seqF >= 1 && !boundedWaitBackoff(barS + 8 * ((seqF - 1) & 1), ((seqF - 1) >> 1) & 1))) {
+                (seqF >= 1 && !boundedWait(barS + 8 * ((seqF - 1) & 1), ((seqF - 1) >> 1) & 1))) {
                 ok = false;
                 break;
             }
@@ -329,7 +329,9 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 dev::tcFenceAfter();
                 const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
                 for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
-                    if (ok && (!boundedWaitBackoff(barA, seq & 1) || !boundedWaitBackoff(barB, seq & 1)))
+                    // With one stage these waits are on the critical path: suspend on the barrier
+                    // (resumes at once) rather than sleep between polls.
+                    if (ok && (!boundedWait(barA, seq & 1) || !boundedWait(barB, seq & 1)))
                         ok = false;
                     if (!ok)
                         continue;
