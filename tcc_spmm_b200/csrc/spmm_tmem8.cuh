@@ -318,12 +318,21 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         if (lane == 0) {
             bool ok = true, issued = false;
             uint32_t seq = 0, windows = 0;
+            // The next task's panel range is loaded one task ahead, off the MMA issue path.
+            uint32_t nextBegin = 0, nextEnd = 0;
+            if (blockIdx.x < matrix.taskCount) {
+                nextBegin = matrix.tasks[blockIdx.x].begin;
+                nextEnd = matrix.tasks[blockIdx.x].end;
+            }
             for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
-                const tcc_sw32_task task = matrix.tasks[tk];
-                const uint32_t panelCount = task.end - task.begin;
+                const uint32_t panelCount = nextEnd - nextBegin;
+                if (tk + gridDim.x < matrix.taskCount) {
+                    nextBegin = matrix.tasks[tk + gridDim.x].begin;
+                    nextEnd = matrix.tasks[tk + gridDim.x].end;
+                }
                 if (panelCount == 0)
                     continue;
-                if (ok && windows >= 1 && !boundedWaitBackoff(barR, (windows - 1) & 1))
+                if (ok && windows >= 1 && !boundedWait(barR, (windows - 1) & 1))
                     ok = false;
                 ++windows;
                 dev::tcFenceAfter();
