@@ -292,8 +292,9 @@ int tcc_launch_spmm_int8(const tcc_sw32_device_view* matrix, const int8_t* packe
 }
 
 // Same contract as tcc_launch_spmm_int8 with an explicit kernel choice (tests and tuning; not
-// part of the public header): 0 default, 1 generic, 2/3 persistent with 32/64-feature
-// consumer warps.
+// part of the public header): 0 default (= 12), 1 generic, 2-7 persistent (32/64-feature consumer
+// warps; 1, 2 or 4 producer warps), 8-11 tensor-memory with 4-panel chunks (stages, producers) =
+// (2, 1), (2, 2), (4, 2), (4, 4), 12 tensor-memory with 8-panel chunks.
 int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_t* packed_x, const float* scales,
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
