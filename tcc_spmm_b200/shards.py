@@ -52,7 +52,7 @@ def assemble_rows(y, ranges: Sequence[tuple], group=None) -> None:
     if len(ranges) != dist.get_world_size(group):
         raise ValueError("one row range per rank")
     pieces = [(r, y[begin:end]) for r, (begin, end) in enumerate(ranges) if end > begin]
-    if y.is_cuda and dist.get_backend(group) == "nccl":
+    if y.is_cuda and dist.get_backend(group) == "nccl" and hasattr(dist, "_coalescing_manager"):
         # One NCCL group: the owners' broadcasts run concurrently, so every link carries data
         # in both directions at once.
         with dist._coalescing_manager(group=group, device=y.device, async_ops=True) as cm:
