@@ -153,8 +153,7 @@ def shard_bytes(fmt, lo: int, hi: int, features: int) -> dict:
     sw0, sw1 = int(t["sw"][0]), int(t["sw"][-1]) + 1
     ids = fmt.source_ids[8 * p0:8 * p1]
     valid = int(np.count_nonzero(ids != 0xFFFFFFFF))
-    v0 = int(fmt.window_offsets[sw0])  # panel offsets; values: count via masks
-    meta = fmt.source_metadata[8 * p0:8 * p1]
+    meta = fmt.source_metadata[8 * p0:8 * p1]  # values: one per set bit of the row masks
     nnz = int(np.bitwise_count(meta & np.uint64(0xFFFFFFFF)).sum())
     rows = min(fmt.rows, 32 * sw1) - 32 * sw0
     split = t[t["partial"] != 0xFFFFFFFF]
@@ -162,7 +161,6 @@ def shard_bytes(fmt, lo: int, hi: int, features: int) -> dict:
     a_bytes += 8 * 4 * len(np.unique(split["sw"])) + 4 * int(sum(bin(int(m)).count("1") for m in split["mask"]))
     x_bytes = valid * (features + 4)
     y_bytes = 4 * rows * features
-    del v0
     return {"total": int(a_bytes + x_bytes + y_bytes), "a_bytes": int(a_bytes), "x_bytes": int(x_bytes),
             "y_bytes": int(y_bytes), "nnz": nnz, "rows": int(rows), "valid_slots": valid, "panels": p1 - p0,
             "row_begin": 32 * sw0, "row_end": min(fmt.rows, 32 * sw1)}

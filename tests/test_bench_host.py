@@ -1,0 +1,51 @@
+"""Host-side logic of bench.py (no GPU): the algorithmic bytes of a task range (the roofline's
+numerator), the window-aligned slices of the end-to-end leg, and the choice of the ncu traffic
+entry that matches the running kernel."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import bench
+import tcc_spmm_b200 as T
+from tcc_spmm_b200 import workloads as W
+
+
+@pytest.fixture(scope="module")
+def fmt():
+    csr = W.generate("stress_small")
+    return T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+
+
+@pytest.mark.parametrize("features", [128, 256])
+def test_whole_range_bytes_equal_format_bytes(fmt, features):
+    assert bench.shard_bytes(fmt, 0, fmt.tasks.size, features)["total"] == fmt.algorithmic_bytes(features)["total"]
+
+
+@pytest.mark.parametrize("parts", [2, 3, 8])
+def test_shard_bytes_add_up(fmt, parts):
+    bounds = T.partition_tasks(fmt, 128, parts)
+    shards = [bench.shard_bytes(fmt, int(bounds[r]), int(bounds[r + 1]), 128) for r in range(parts)]
+    full = bench.shard_bytes(fmt, 0, fmt.tasks.size, 128)
+    for key in ("total", "a_bytes", "x_bytes", "y_bytes", "nnz", "rows", "valid_slots", "panels"):
+        assert sum(s.get(key, 0) for s in shards) == full[key], key
+
+
+@pytest.mark.parametrize("parts", [1, 4, 8, 64])
+def test_window_cuts_start_at_window_boundaries(fmt, parts):
+    n = fmt.tasks.size
+    cuts = bench.window_cuts(fmt, 0, n, parts)
+    assert cuts[0] == 0 and cuts[-1] == n and cuts == sorted(set(cuts))
+    sw = fmt.tasks["sw"]
+    assert all(sw[c] != sw[c - 1] for c in cuts[1:-1])
+
+
+def test_traffic_entry_matches_launch_shape():
+    entry = bench.profile_traffic("powerlaw128", "default", "balanced")
+    assert entry is not None and entry["dram_bytes_per_launch"] > 0
+    same = dict(entry["launch"])
+    assert bench.profile_traffic("powerlaw128", "default", "balanced", same) is not None
+    other = dict(same, smem=same["smem"] + 128)
+    assert bench.profile_traffic("powerlaw128", "default", "balanced", other) is None
+    assert bench.profile_traffic("powerlaw128", "default", "format") is None
+    assert bench.profile_traffic("powerlaw128", "generic", "balanced") is None
