@@ -162,6 +162,16 @@ __device__ __forceinline__ void cpAsync16Hint(uint32_t dst, const void* src, uin
                  "r"(srcBytes), "l"(policy)
                  : "memory");
 }
+// 16-byte async copy with a 128-byte L2 prefetch of the enclosing line and the default L2
+// policy; srcBytes 0 writes zeros.
+__device__ __forceinline__ void cpAsync16Line(uint32_t dst, const void* src, uint32_t srcBytes) {
+    asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(srcBytes)
+                 : "memory");
+}
+// 16 zero bytes to shared memory (16-byte aligned address).
+__device__ __forceinline__ void stsZero16(uint32_t addr) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+}
 __device__ __forceinline__ void cpAsync4Hint(uint32_t dst, const void* src, uint32_t srcBytes, uint64_t policy) {
     asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2, %3;" ::"r"(dst), "l"(src), "r"(srcBytes),
                  "l"(policy)

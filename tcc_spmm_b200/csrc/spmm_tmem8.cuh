@@ -31,6 +31,11 @@
 // stored), sFree[c % 2] (MMA commit of chunk c -> the producer and the consumers of chunk c + 1,
 // who then refill the B tiles and the A columns at the same time), dFull/dFree for the
 // accumulator, aLand/aUsed and vFull for the producer rings. All waits bounded.
+// Every copy uses the default L2 policy: evict-last on X and evict-first on the format arrays
+// cost 3%. The X copies keep the 128-byte L2 prefetch. Invalid slots issue no copy at all: the
+// consumer stores zeros to shared memory, and the producer skips their scales. A zero-size copy
+// from one shared dummy address per invalid slot made every SM queue on that one address (5%
+// slower on power-law F128; for the scales 2%), and a full copy of a dummy row 60%.
 #pragma once
 #include "spmm_tmem.cuh"
 
@@ -93,12 +98,12 @@ __device__ __forceinline__ uint32_t xRowSlot(uint32_t row) {
 }
 
 // Consumer X step of chunk s: warp w gathers bytes 32w..32w+31 of the chunk's 64 packed source
-// rows (two 16-byte cp.async per row, invalid slots zero-filled) as one cp.async group, then
+// rows (two 16-byte cp.async per row; zeros stored for invalid slots) as one cp.async group, then
 // tells the producer that the chunk's IDs have been read. Returns false when the wait ran out.
 template <int F, int P>
 __device__ __forceinline__ bool gatherSlice8(unsigned char* smem, uint32_t xring, uint32_t barLand, uint32_t barUsed,
                                              const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
-                                             uint32_t s, int lane, int w, uint64_t policy, bool ok) {
+                                             uint32_t s, int lane, int w, bool ok) {
     using L = Tmem8<F, P>;
     if (ok && s < total) {
         const uint32_t aslot = s % L::kARing;
@@ -112,11 +117,11 @@ __device__ __forceinline__ bool gatherSlice8(unsigned char* smem, uint32_t xring
             for (int pass = 0; pass < 4; ++pass) {
                 const uint32_t row = pass * 16 + (lane >> 1), piece = lane & 1;
                 const uint32_t id = (row >> 3) < np ? reinterpret_cast<const uint32_t*>(a)[row] : 0xFFFFFFFFu;
-                const bool valid = id < cols;
-                dev::cpAsync16Hint(dst + xRowSlot(row) * 32 + 16 * piece,
-                                   valid ? static_cast<const void*>(packedX + uint64_t(id) * F + 32 * w + 16 * piece)
-                                         : static_cast<const void*>(packedX),
-                                   valid ? 16u : 0u, policy);
+                const uint32_t d = dst + xRowSlot(row) * 32 + 16 * piece;
+                if (id < cols)
+                    dev::cpAsync16Line(d, packedX + uint64_t(id) * F + 32 * w + 16 * piece, 16u);
+                else
+                    dev::stsZero16(d);
             }
             __syncwarp();
             if (lane == 0)
@@ -178,8 +183,6 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
 
     if (warp >= L::kProducerWarp && warp < L::kMmaWarp) {
         // =================================== producers ====================================
-        const uint64_t polStream = dev::policyEvictFirst();
-        const uint64_t polKeep = dev::policyEvictLast();
         uint32_t* vBase = reinterpret_cast<uint32_t*>(smem + L::kVBaseOff);
         const uint32_t pw = warp - L::kProducerWarp;
         ChunkWalkerT<kChunk8> walk;
@@ -206,9 +209,9 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                     header[1] = np;
                     dev::fenceProxyAsyncShared(); // earlier generic reads of the slot before the copies
                     dev::mbarArriveExpectTx(barL + 8 * slot, 96 * np);
-                    dev::bulkCopyG2SHint(a, matrix.sourceIds + uint64_t(p0) * 8, 32 * np, barL + 8 * slot, polStream);
-                    dev::bulkCopyG2SHint(a + 4 * L::kSlots, matrix.sourceMetadata + uint64_t(p0) * 8, 64 * np,
-                                         barL + 8 * slot, polStream);
+                    dev::bulkCopyG2S(a, matrix.sourceIds + uint64_t(p0) * 8, 32 * np, barL + 8 * slot);
+                    dev::bulkCopyG2S(a + 4 * L::kSlots, matrix.sourceMetadata + uint64_t(p0) * 8, 64 * np,
+                                     barL + 8 * slot);
                 }
 #pragma unroll
                 for (int i = 0; i < P; ++i)
@@ -235,10 +238,8 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                     const uint32_t id = inRange ? reinterpret_cast<const uint32_t*>(a)[slot] : 0xFFFFFFFFu;
                     const uint64_t meta =
                         inRange ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
-                    const bool valid = id < cols;
-                    dev::cpAsync4Hint(dev::smemAddr(v + 4 * L::kVCap + 4 * slot),
-                                      valid ? static_cast<const void*>(scales + id) : static_cast<const void*>(scales),
-                                      valid ? 4u : 0u, polKeep);
+                    if (id < cols) // an invalid slot's scale is never read (its row mask is empty)
+                        dev::cpAsync4(dev::smemAddr(v + 4 * L::kVCap + 4 * slot), scales + id, 4u);
                     const uint32_t mask = static_cast<uint32_t>(meta);
                     const uint32_t first = static_cast<uint32_t>(meta >> 32);
                     if (mask) {
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                     vBase[vslot] = count <= uint32_t(L::kVCap) ? lo : 0xFFFFFFFFu;
                 if (count <= uint32_t(L::kVCap))
                     for (uint32_t i = lane; i < count; i += 32)
-                        dev::cpAsync4Hint(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4, polStream);
+                        dev::cpAsync4(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4);
                 dev::cpAsyncArriveNoinc(barV + 8 * vslot);
             }
             if (!ok)
@@ -372,7 +373,6 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         // ==================================== consumers ===================================
         const int quarter = warp & 3, slice = warp >> 2;
         const int g = lane >> 2, c = lane & 3;
-        const uint64_t polKeep = dev::policyEvictLast();
         const uint32_t xring = base + L::kXOff + warp * L::kXDepth * L::kXSlotBytes;
         const uint32_t tLane = uint32_t(32 * quarter) << 16;
         const uint32_t aTmem = tmem + slice * L::kSliceCols + tLane;
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         const uint32_t xLane = xring + 4 * g + 32 * c;
         bool ok = true;
         for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
-            ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, polKeep, ok);
+            ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, ok);
         uint32_t seq = 0, windows = 0;
         tcc_sw32_task nextTask{};
         if (blockIdx.x < matrix.taskCount)
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
                 ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, warp,
-                                        polKeep, ok);
+                                        ok);
                 dev::cpAsyncWaitGroup<L::kPrefetch>();
                 __syncwarp();
                 // The MMAs of chunk seq - 1 are complete: the A columns may be rewritten (the
