@@ -141,11 +141,8 @@ __device__ __forceinline__ void cpAsync4(uint32_t dst, const void* src, uint32_t
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(srcBytes)
                  : "memory");
 }
-// 16-byte async copy through L2 only (no L1 allocation); srcBytes 0 writes zeros.
-__device__ __forceinline__ void cpAsync16(uint32_t dst, const void* src, uint32_t srcBytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(srcBytes) : "memory");
-}
-// L2 eviction policies (createpolicy): keep the gathered feature rows, stream the format.
+// L2 eviction policies (createpolicy): keep the gathered feature rows, stream the format. Used
+// by the 4-panel and mma.sync kernels; the 8-panel default kernel runs faster without them.
 __device__ __forceinline__ uint64_t policyEvictLast() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -184,9 +181,6 @@ __device__ __forceinline__ void cpAsync8Hint(uint32_t dst, const void* src, uint
 __device__ __forceinline__ void cpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cpAsyncWaitGroup() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void cpAsync8(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cpAsyncWaitAll() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // Bulk (TMA engine) copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
