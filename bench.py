@@ -57,7 +57,8 @@ def parse_args():
                    help="launch the tasks in format order instead of the balanced order (tcc_balance_tasks)")
     p.add_argument("--variant", default="default",
                    choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
-                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4", "tmem8"],
+                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4", "tmem8",
+                            "tmem8w"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()
@@ -418,7 +419,7 @@ def run_tcc(args):
     lo, hi = int(bounds[rank]), int(bounds[rank + 1])
     shard = shard_bytes(fmt, lo, hi, F)
     full = fmt.algorithmic_bytes(F)
-    dm = T.DeviceMatrix(fmt, F, device, task_range=(lo, hi), balance=not args.natural_order)
+    dm = T.DeviceMatrix(fmt, F, device, task_range=(lo, hi), balance=not args.natural_order, variant=args.variant)
     x = W.normal_features(fmt.cols, F, threads=threads)
     xd = torch.from_numpy(x).to(device)
     packed = torch.empty(fmt.cols * F, dtype=torch.int8, device=device)

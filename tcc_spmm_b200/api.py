@@ -293,11 +293,12 @@ class DeviceMatrix:
     windows*(F/128) zeroed u32 when partialCount > 0.
 
     balance=True also uploads the tasks in the order of balance_tasks for the grid of the
-    default kernel on this device; view() of the whole task range then uses that order
-    (sub-range views keep the natural order, whose ranges cover contiguous windows)."""
+    kernel `variant` (the default kernel unless named) on this device; view() of the whole task
+    range then uses that order (sub-range views keep the natural order, whose ranges cover
+    contiguous windows)."""
 
     def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None,
-                 balance: bool = False):
+                 balance: bool = False, variant: str = "default"):
         import torch
 
         self.rows, self.cols, self.features = fmt.rows, fmt.cols, features
@@ -320,7 +321,8 @@ class DeviceMatrix:
         self.tasks_balanced = None
         if balance and self.task_count:
             with torch.cuda.device(self.device):
-                grid = spmm_launch_shape(features)["grid"]
+                # The generic kernel's grid is per call (reported as 0): balance for the default's.
+                grid = spmm_launch_shape(features, variant)["grid"] or spmm_launch_shape(features)["grid"]
             order = balance_tasks(tasks, fmt.row_group_masks, features, grid)
             self.tasks_balanced = up(order.view(np.uint32), torch.int32)
         self.reductions = up(np.ascontiguousarray(fmt.reductions).view(np.uint32), torch.int32)
@@ -501,7 +503,7 @@ def _np_of(torch_dtype):
 
 KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "persistent32x2": 4,
                    "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7, "tmem2p1": 8, "tmem2p2": 9,
-                   "tmem4p2": 10, "tmem4p4": 11, "tmem8": 12}
+                   "tmem4p2": 10, "tmem4p4": 11, "tmem8": 12, "tmem8w": 13}
 
 
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,

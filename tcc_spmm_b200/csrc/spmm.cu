@@ -14,6 +14,8 @@
 //     sourceMetadata are 16-byte aligned (always true for cudaMalloc'd buffers).
 //   spmmTmemKernel (spmm_tmem.cuh): the same arithmetic with 4-panel chunks and two stages
 //     (variants 8-11).
+//   spmmTmem8WKernel (spmm_tmem8w.cuh): the 8-panel kernel with two consumer warps per TMEM
+//     lane quarter and three producer warps, F = 128 only (variant 13, experimental).
 //   spmmPersistentKernel (spmm_persistent.cuh): mma.sync with register accumulators, when
 //     only the IDs or metadata are not 16-byte aligned.
 //   spmmGenericKernel (spmm_generic.cuh): any 2-byte aligned packedX (the reference's own
@@ -25,6 +27,7 @@
 #include "spmm_persistent.cuh"
 #include "spmm_tmem.cuh"
 #include "spmm_tmem8.cuh"
+#include "spmm_tmem8w.cuh"
 
 #include <algorithm>
 #include <cuda_runtime.h>
@@ -131,6 +134,9 @@ template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
 template <int F, int P> LaunchShape tmem8Shape(int device) {
     return tmemShapeOf<Tmem8<F, P>, spmmTmem8Kernel<F, P>>(device);
 }
+template <int F, int P> LaunchShape tmem8wShape(int device) {
+    return tmemShapeOf<Tmem8W<F, P>, spmmTmem8WKernel<F, P>>(device);
+}
 
 template <int F, int P>
 void launchTmem8(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
@@ -141,6 +147,17 @@ void launchTmem8(const tcc_sw32_device_view& m, const int8_t* x, const float* sc
     const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
     spmmTmem8Kernel<F, P><<<grid, Tmem8<F, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols, partials,
                                                                            counters);
+}
+
+template <int F, int P>
+void launchTmem8W(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
+                  uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
+    int device = 0;
+    throwIf(cudaGetDevice(&device));
+    const LaunchShape s = tmem8wShape<F, P>(device);
+    const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
+    spmmTmem8WKernel<F, P><<<grid, Tmem8W<F, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols, partials,
+                                                                             counters);
 }
 
 template <int F, int STAGES, int P>
@@ -158,7 +175,8 @@ void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* sca
 // features per consumer warp and one producer warp, 4/5 = the same with two producer warps,
 // 6/7 = with four producer warps, 8..11 = tensor-memory kernel with (stages, producer warps)
 // (2, 1), (2, 2), (4, 2), (4, 4), 12 = tensor-memory kernel with 8-panel chunks, one stage and
-// two producer warps.
+// two producer warps, 13 = the same with two consumer warps per TMEM lane quarter and three
+// producer warps (F = 128 only; checked by the caller).
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
@@ -193,6 +211,9 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
         launchTmem<F, 4, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else if (variant == 11) {
         launchTmem<F, 4, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
+    } else if (variant == 13) {
+        if constexpr (F == 128)
+            launchTmem8W<F, 3>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else {
         launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
@@ -294,13 +315,16 @@ int tcc_launch_spmm_int8(const tcc_sw32_device_view* matrix, const int8_t* packe
 // Same contract as tcc_launch_spmm_int8 with an explicit kernel choice (tests and tuning; not
 // part of the public header): 0 default (= 12), 1 generic, 2-7 persistent (32/64-feature consumer
 // warps; 1, 2 or 4 producer warps), 8-11 tensor-memory with 4-panel chunks (stages, producers) =
-// (2, 1), (2, 2), (4, 2), (4, 4), 12 tensor-memory with 8-panel chunks.
+// (2, 1), (2, 2), (4, 2), (4, 4), 12 tensor-memory with 8-panel chunks, 13 the same with two
+// consumer warps per lane quarter and three producer warps (F = 128 only; experimental).
 int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_t* packed_x, const float* scales,
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
     return tcc::guarded([&] {
-        if (variant < 0 || variant > 12)
+        if (variant < 0 || variant > 13)
             throw std::invalid_argument("unknown SpMM kernel variant");
+        if (variant == 13 && features != 128)
+            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
         tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters,
                            reinterpret_cast<cudaStream_t>(stream), variant);
     });
@@ -316,8 +340,10 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             throw std::invalid_argument("null output");
         if (features != 128 && features != 256)
             throw std::invalid_argument("feature dimension must be 128 or 256");
-        if (variant < 0 || variant > 12)
+        if (variant < 0 || variant > 13)
             throw std::invalid_argument("unknown SpMM kernel variant");
+        if (variant == 13 && features != 128)
+            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
         int device = 0, sms = 1;
         tcc::throwIf(cudaGetDevice(&device));
         tcc::throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
@@ -348,6 +374,7 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             case 10: tmem(tcc::Tmem<128, 4, 2>{}, tcc::tmemShape<128, 4, 2>(device)); break;
             case 11: tmem(tcc::Tmem<128, 4, 4>{}, tcc::tmemShape<128, 4, 4>(device)); break;
             case 12: tmem(tcc::Tmem8<128, 2>{}, tcc::tmem8Shape<128, 2>(device)); break;
+            case 13: tmem(tcc::Tmem8W<128, 3>{}, tcc::tmem8wShape<128, 3>(device)); break;
             default: break;
             }
         } else {

@@ -238,6 +238,12 @@ __device__ __forceinline__ void tcStore16x256bx4(uint32_t taddr, const uint32_t 
                  "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
                  : "memory");
 }
+// The same store with 2 repetitions (16 columns, 8 registers per thread).
+__device__ __forceinline__ void tcStore16x256bx2(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
 // Warp load of 32 TMEM lanes x 16 columns (32x32b shape, 16 repetitions): thread t reads
 // lane t, r[j] = column j.
 __device__ __forceinline__ void tcLoad32x32bx16(uint32_t taddr, uint32_t (&r)[16]) {

@@ -1,0 +1,506 @@
+// Tensor-memory SpMM kernel with 8-panel chunks and two consumer warps per TMEM lane quarter
+// (tcgen05, sm_100a). Experimental variant 13.
+//
+// The arithmetic, chunking, data layout and hand-offs are those of spmm_tmem8.cuh (see there).
+// What differs is the number of warps that do the consumers' work. An instrumented copy of the
+// 8-panel kernel showed the consumer warps as its critical role: they never wait, the MMA
+// thread waits for their A columns in every chunk, and they run at about 10 cycles per
+// instruction. At 4 CTAs of 7 warps and 72 registers the register file holds no more warps.
+// Here each TMEM lane quarter has two consumer warps: warp w (w < 8) takes quarter w % 4 and
+// half (w / 4) % 2 of every chunk. It gathers its 32-byte column block of the half's 32 source
+// rows, converts the half's 4 panels into A columns 32h..32h+31, and writes rows 16h..16h+15
+// of the window in the epilogue. P = 3 producer warps share the B builds (chunk c's MMA commit
+// goes to sFree[c % P]), so the producers keep pace with the faster consumers. A CTA has 12
+// warps and 3 CTAs share an SM (at most 56 registers per thread); F = 128 only.
+//
+// Not yet run on a GPU.
+#pragma once
+#include "spmm_tmem8.cuh"
+
+namespace tcc {
+namespace {
+
+template <int F, int P> struct Tmem8W {
+    static_assert(F == 128, "the two-warps-per-quarter form is built for F = 128 (3 CTAs per SM)");
+    static_assert(P >= 1 && P <= 3, "sFree[c % P] gives each producer consecutive phases of one barrier");
+    static constexpr int kSlices = F / 128;
+    static constexpr int kHalves = 2;                    // consumer warps per TMEM lane quarter
+    static constexpr int kConsumers = kHalves * F / 32;  // warp w: quarter w % 4, half (w / 4) % 2
+    static constexpr int kProducers = P;
+    static constexpr int kProducerWarp = kConsumers;
+    static constexpr int kMmaWarp = kConsumers + P;
+    static constexpr int kThreads = 32 * (kConsumers + P + 1);
+    static constexpr int kCtasPerSm = 3;                 // the register file holds 3 CTAs of 12 warps
+    static constexpr int kSlots = 8 * kChunk8;
+    static constexpr int kHalfRows = kSlots / kHalves;   // source rows a consumer warp gathers per chunk
+    // Consumer X rings (one per consumer warp): 32 rows x 32 bytes per chunk.
+    static constexpr int kXDepth = 3;
+    static constexpr int kPrefetch = kXDepth - 1;
+    static constexpr int kXSlotBytes = kHalfRows * 32;
+    // Producer rings; every slot belongs to one producer (sizes are multiples of P).
+    static constexpr int kALead = 5, kVLead = 3;
+    static constexpr int kARing = P * ((kALead + 2 + P - 1) / P);
+    static constexpr int kVRing = P * ((kVLead + 1 + P - 1) / P);
+    static constexpr int kVCap = 256;
+    static constexpr int kHeaderOff = 4 * kSlots + 8 * kSlots;  // after ids and metadata
+    static constexpr int kASlotBytes = kHeaderOff + 16;
+    static constexpr int kVSlotBytes = kVCap * 4 + 4 * kSlots; // values, scales
+    static constexpr int kBTileBytes = 2048;
+    static constexpr int kBOff = 0;
+    static constexpr int kXOff = kBOff + kChunk8 * kBTileBytes;
+    static constexpr int kAOff = kXOff + kConsumers * kXDepth * kXSlotBytes;
+    static constexpr int kVOff = kAOff + kARing * kASlotBytes;
+    static constexpr int kVBaseOff = kVOff + kVRing * kVSlotBytes;
+    static constexpr int kFlagOff = kVBaseOff + 4 * kVRing;
+    static constexpr int kBarOff = (kFlagOff + 16 + 7) / 8 * 8;
+    // bFull, aFull, sFree [P] (by chunk mod P), dFull, dFree, aLand [kARing], aUsed [kARing],
+    // vFull [kVRing], drain
+    static constexpr int kBars = 2 + P + 2 + 2 * kARing + kVRing + 1;
+    static constexpr int kBytes = kBarOff + 8 * kBars;
+    // Tensor memory: the A stage (64 columns: 8 panels x 8 sources) and the accumulator (64).
+    static constexpr int kSliceCols = 8 * kChunk8 + 64;
+    static constexpr int kColsUsed = kSlices * kSliceCols;
+    static constexpr int kTmemCols = 128;
+    static constexpr int kMaxCtasPerSm = 512 / kTmemCols;
+    static_assert(kColsUsed <= kTmemCols, "tensor memory");
+    static_assert(kVRing <= 8 && kARing >= kALead + 2 && kVRing > kVLead && kALead > kVLead && kPrefetch <= kALead,
+                  "rings");
+    static_assert(kARing % P == 0 && kVRing % P == 0, "every ring slot has one producer");
+    static_assert(kASlotBytes % 16 == 0 && kXOff % 16 == 0 && kAOff % 16 == 0 && kVOff % 16 == 0 && kBarOff % 8 == 0,
+                  "alignment");
+    static constexpr uint32_t kIdesc = Tmem<F, 2, 2>::kIdesc;
+};
+
+// Consumer X step of chunk s: the warp of quarter q and half h gathers bytes 32q..32q+31 of the
+// chunk's source rows 32h..32h+31 (panels 4h..4h+3; two 16-byte cp.async per row, zeros stored
+// for invalid slots) as one cp.async group, then tells the producer that it has read the IDs.
+// Returns false when the wait ran out.
+template <int F, int P>
+__device__ __forceinline__ bool gatherHalf8(unsigned char* smem, uint32_t xring, uint32_t barLand, uint32_t barUsed,
+                                            const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
+                                            uint32_t s, int lane, int q, int h, bool ok) {
+    using L = Tmem8W<F, P>;
+    if (ok && s < total) {
+        const uint32_t aslot = s % L::kARing;
+        if (!boundedWait(barLand + 8 * aslot, (s / L::kARing) & 1)) {
+            ok = false;
+        } else {
+            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+            const uint32_t dst = xring + (s % L::kXDepth) * L::kXSlotBytes;
+#pragma unroll
+            for (int pass = 0; pass < L::kHalfRows / 16; ++pass) {
+                const uint32_t local = pass * 16 + (lane >> 1), piece = lane & 1;
+                const uint32_t row = L::kHalfRows * h + local;
+                const uint32_t id = (row >> 3) < np ? reinterpret_cast<const uint32_t*>(a)[row] : 0xFFFFFFFFu;
+                const uint32_t d = dst + xRowSlot(local) * 32 + 16 * piece;
+                if (id < cols)
+                    dev::cpAsync16Line(d, packedX + uint64_t(id) * F + 32 * q + 16 * piece, 16u);
+                else
+                    dev::stsZero16(d);
+            }
+            __syncwarp();
+            if (lane == 0)
+                dev::mbarArrive(barUsed + 8 * aslot);
+        }
+    }
+    dev::cpAsyncCommit();
+    return ok;
+}
+
+template <int F, int P>
+__global__ void __launch_bounds__(Tmem8W<F, P>::kThreads, Tmem8W<F, P>::kCtasPerSm)
+    spmmTmem8WKernel(const tcc_sw32_device_view matrix, const int8_t* __restrict__ packedX,
+                     const float* __restrict__ scales, float* __restrict__ output, uint32_t rows, uint32_t cols,
+                     float* __restrict__ partials, uint32_t* __restrict__ counters) {
+    using L = Tmem8W<F, P>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = dev::smemAddr(smem);
+    const uint32_t barB = base + L::kBarOff;   // bFull
+    const uint32_t barA = barB + 8;            // aFull
+    const uint32_t barS = barA + 8;            // sFree [P]
+    const uint32_t barD = barS + 8 * P;        // dFull
+    const uint32_t barR = barD + 8;            // dFree
+    const uint32_t barL = barR + 8;            // aLand [kARing]
+    const uint32_t barU = barL + 8 * L::kARing; // aUsed [kARing]
+    const uint32_t barV = barU + 8 * L::kARing; // vFull [kVRing]
+    const uint32_t barF = barV + 8 * L::kVRing; // drain
+    volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(smem + L::kFlagOff);
+    if (threadIdx.x == 0) {
+        dev::mbarInit(barB, 1);
+        dev::mbarInit(barA, L::kConsumers);
+        for (int p = 0; p < P; ++p)
+            dev::mbarInit(barS + 8 * p, 1);
+        dev::mbarInit(barD, 1);
+        dev::mbarInit(barR, L::kConsumers);
+        for (int s = 0; s < L::kARing; ++s) {
+            dev::mbarInit(barL + 8 * s, 1);
+            dev::mbarInit(barU + 8 * s, L::kConsumers);
+        }
+        for (int s = 0; s < L::kVRing; ++s)
+            dev::mbarInit(barV + 8 * s, 32);
+        dev::mbarInit(barF, 1);
+        flags[0] = flags[1] = flags[3] = 0; // flags[2] receives the TMEM address (allocating warp)
+        dev::fenceBarrierInit();
+    }
+    if (warp == L::kMmaWarp) {
+        dev::tmemAlloc(base + L::kFlagOff + 8, L::kTmemCols);
+        dev::tmemRelinquish();
+    }
+    dev::tcFenceBefore();
+    __syncthreads();
+    dev::tcFenceAfter();
+    const uint32_t tmem = flags[2];
+    const uint32_t total = ctaChunkCountT<kChunk8>(matrix, lane);
+
+    if (warp >= L::kProducerWarp && warp < L::kMmaWarp) {
+        // =================================== producers ====================================
+        uint32_t* vBase = reinterpret_cast<uint32_t*>(smem + L::kVBaseOff);
+        const uint32_t pw = warp - L::kProducerWarp;
+        ChunkWalkerT<kChunk8> walk;
+        walk.start(matrix);
+        for (uint32_t i = 0; i < pw; ++i)
+            walk.advance(matrix);
+        uint32_t seqA = pw, seqV = pw;
+        bool ok = true;
+        for (uint32_t seqF = pw; seqF < total && ok; seqF += P) {
+            // ---- A steps: IDs and metadata of chunks up to seqF + kALead (one lane) ----
+            for (; seqA < total && seqA <= seqF + L::kALead; seqA += P) {
+                const uint32_t slot = seqA % L::kARing;
+                if (seqA >= uint32_t(L::kARing) && !boundedWait(barU + 8 * slot, ((seqA / L::kARing) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t p0 = walk.next;
+                const uint32_t np = min(uint32_t(kChunk8), walk.end - p0);
+                if (lane == 0) {
+                    const uint32_t a = base + L::kAOff + slot * L::kASlotBytes;
+                    uint32_t* header =
+                        reinterpret_cast<uint32_t*>(smem + L::kAOff + slot * L::kASlotBytes + L::kHeaderOff);
+                    header[0] = p0;
+                    header[1] = np;
+                    dev::fenceProxyAsyncShared(); // earlier generic reads of the slot before the copies
+                    dev::mbarArriveExpectTx(barL + 8 * slot, 96 * np);
+                    dev::bulkCopyG2S(a, matrix.sourceIds + uint64_t(p0) * 8, 32 * np, barL + 8 * slot);
+                    dev::bulkCopyG2S(a + 4 * L::kSlots, matrix.sourceMetadata + uint64_t(p0) * 8, 64 * np,
+                                     barL + 8 * slot);
+                }
+#pragma unroll
+                for (int i = 0; i < P; ++i)
+                    walk.advance(matrix);
+            }
+            if (!ok)
+                break;
+            __syncwarp();
+            // ---- V steps: value ranges and scales of chunks up to seqF + kVLead ----
+            for (; seqV < seqA && seqV <= seqF + L::kVLead; seqV += P) {
+                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing;
+                if (!boundedWait(barL + 8 * aslot, (seqV / L::kARing) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+                unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
+                const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+                uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t slot = lane + 32 * h;
+                    const bool inRange = (slot >> 3) < np;
+                    const uint32_t id = inRange ? reinterpret_cast<const uint32_t*>(a)[slot] : 0xFFFFFFFFu;
+                    const uint64_t meta =
+                        inRange ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
+                    if (id < cols) // an invalid slot's scale is never read (its row mask is empty)
+                        dev::cpAsync4(dev::smemAddr(v + 4 * L::kVCap + 4 * slot), scales + id, 4u);
+                    const uint32_t mask = static_cast<uint32_t>(meta);
+                    const uint32_t first = static_cast<uint32_t>(meta >> 32);
+                    if (mask) {
+                        lo = min(lo, first);
+                        hi = max(hi, first + __popc(mask));
+                    }
+                }
+                lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+                hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+                const uint32_t count = hi > lo ? hi - lo : 0u;
+                if (lane == 0)
+                    vBase[vslot] = count <= uint32_t(L::kVCap) ? lo : 0xFFFFFFFFu;
+                if (count <= uint32_t(L::kVCap))
+                    for (uint32_t i = lane; i < count; i += 32)
+                        dev::cpAsync4(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4);
+                dev::cpAsyncArriveNoinc(barV + 8 * vslot);
+            }
+            if (!ok)
+                break;
+            // ---- B step: the B tiles of chunk seqF, once the MMAs of chunk seqF - 1 are done.
+            // Chunk c's commit goes to sFree[c % P], so each producer waits on consecutive
+            // phases of one barrier (the parity of a phase two ahead would be ambiguous). ----
+            const uint32_t aslot = seqF % L::kARing, vslot = seqF % L::kVRing;
+            if (!boundedWait(barV + 8 * vslot, (seqF / L::kVRing) & 1) ||
+                (seqF >= 1 && !boundedWait(barS + 8 * ((seqF - 1) % P), ((seqF - 1) / P) & 1))) {
+                ok = false;
+                break;
+            }
+            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+            const unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
+            const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
+            unsigned char* tiles = smem + L::kBOff;
+            {
+                uint4* z = reinterpret_cast<uint4*>(tiles);
+#pragma unroll
+                for (int i = 0; i < kChunk8 * L::kBTileBytes / 16 / 32; ++i)
+                    z[i * 32 + lane] = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+            const uint32_t vb = vBase[vslot];
+            const float* vsm = reinterpret_cast<const float*>(v);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t slot = lane + 32 * h;
+                const uint32_t pp = slot >> 3, k = slot & 7;
+                const uint64_t meta = pp < np ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
+                const float scale = reinterpret_cast<const float*>(v + 4 * L::kVCap)[slot];
+                uint32_t mask = static_cast<uint32_t>(meta);
+                const uint32_t first = static_cast<uint32_t>(meta >> 32);
+                uint32_t* tile = reinterpret_cast<uint32_t*>(tiles + pp * L::kBTileBytes + (k >> 2) * 128 + (k & 3) * 4);
+                uint32_t j = 0;
+                while (mask) {
+                    const int r = __ffs(mask) - 1;
+                    mask &= mask - 1;
+                    const float value = vb != 0xFFFFFFFFu ? vsm[first + j - vb] : __ldg(matrix.values + first + j);
+                    ++j;
+                    const float b = __uint_as_float(dev::tf32Exact(value)) * scale;
+                    const uint32_t bh = dev::tf32Exact(b);
+                    const uint32_t bl = dev::tf32Exact(b - __uint_as_float(bh));
+                    tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = bh;
+                    tile[((r & 7) * 16 + (r >> 3) * 256 + 1024) / 4] = bl;
+                }
+            }
+            dev::fenceProxyAsyncShared();
+            __syncwarp();
+            if (lane == 0)
+                dev::mbarArrive(barB);
+        }
+        if (!ok)
+            flags[1] = 1;
+        dev::cpAsyncWaitAll();
+        // No bulk copy may still be writing into this CTA's shared memory at exit.
+        for (uint32_t s = seqA >= L::kARing + pw ? seqA - L::kARing : pw; s < seqA; s += P)
+            boundedWait(barL + 8 * (s % L::kARing), (s / L::kARing) & 1);
+    } else if (warp == L::kMmaWarp) {
+        // ================================ MMA issuer (one thread) =========================
+        if (lane == 0) {
+            bool ok = true, issued = false;
+            uint32_t seq = 0, windows = 0;
+            // The next task's panel range is loaded one task ahead, off the MMA issue path.
+            uint32_t nextBegin = 0, nextEnd = 0;
+            if (blockIdx.x < matrix.taskCount) {
+                nextBegin = matrix.tasks[blockIdx.x].begin;
+                nextEnd = matrix.tasks[blockIdx.x].end;
+            }
+            for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
+                const uint32_t panelCount = nextEnd - nextBegin;
+                if (tk + gridDim.x < matrix.taskCount) {
+                    nextBegin = matrix.tasks[tk + gridDim.x].begin;
+                    nextEnd = matrix.tasks[tk + gridDim.x].end;
+                }
+                if (panelCount == 0)
+                    continue;
+                if (ok && windows >= 1 && !boundedWait(barR, (windows - 1) & 1))
+                    ok = false;
+                ++windows;
+                dev::tcFenceAfter();
+                const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
+                for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                    // With one stage these waits are on the critical path: suspend on the barrier
+                    // (resumes at once) rather than sleep between polls.
+                    if (ok && (!boundedWait(barA, seq & 1) || !boundedWait(barB, seq & 1)))
+                        ok = false;
+                    if (!ok)
+                        continue;
+                    dev::tcFenceAfter();
+                    const uint32_t inChunk = min(uint32_t(kChunk8), panelCount - ch * kChunk8);
+                    for (uint32_t pp = 0; pp < inChunk; ++pp) {
+                        const unsigned long long desc = bTileDesc(base + L::kBOff + pp * L::kBTileBytes);
+#pragma unroll
+                        for (int sl = 0; sl < L::kSlices; ++sl)
+                            dev::mmaTf32Ts(tmem + sl * L::kSliceCols + 8 * kChunk8, tmem + sl * L::kSliceCols + 8 * pp,
+                                           desc, L::kIdesc, (ch | pp) != 0);
+                    }
+                    issued = true;
+                    dev::tcCommit(barS + 8 * (seq % P));
+                }
+                if (ok)
+                    dev::tcCommit(barD);
+            }
+            if (issued) { // every MMA is complete before the tensor memory is released
+                dev::tcCommit(barF);
+                if (!boundedWait(barF, 0))
+                    ok = false;
+            }
+            if (!ok)
+                flags[1] = 1;
+        }
+        __syncwarp();
+    } else {
+        // ==================================== consumers ===================================
+        const int quarter = warp & 3, half = (warp >> 2) & 1, slice = warp >> 3;
+        const int g = lane >> 2, c = lane & 3;
+        const uint32_t xring = base + L::kXOff + warp * L::kXDepth * L::kXSlotBytes;
+        const uint32_t tLane = uint32_t(32 * quarter) << 16;
+        const uint32_t aTmem = tmem + slice * L::kSliceCols + tLane;
+        const uint32_t dTmem = tmem + slice * L::kSliceCols + 8 * kChunk8 + tLane;
+        const uint32_t feature = slice * 128 + 32 * quarter + tmemLaneFeature(lane);
+        const int q = 4 * slice + quarter; // 32-byte column block of the packed X rows
+        // Rows 2c and 2c + 1 of panel pp sit at positions 8pp + c and 8pp + 4 + c.
+        const uint32_t xLane = xring + 4 * g + 32 * c;
+        bool ok = true;
+        for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
+            ok = gatherHalf8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, q, half, ok);
+        uint32_t seq = 0, windows = 0;
+        tcc_sw32_task nextTask{};
+        if (blockIdx.x < matrix.taskCount)
+            nextTask = matrix.tasks[blockIdx.x];
+        for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
+            const tcc_sw32_task task = nextTask;
+            if (tk + gridDim.x < matrix.taskCount)
+                nextTask = matrix.tasks[tk + gridDim.x];
+            const uint32_t panelCount = task.end - task.begin;
+            const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
+            for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                ok = gatherHalf8<F, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, q,
+                                       half, ok);
+                dev::cpAsyncWaitGroup<L::kPrefetch>();
+                __syncwarp();
+                // The MMAs of chunk seq - 1 are complete: the A columns may be rewritten (the
+                // producer refills the B tiles at the same time).
+                if (ok && seq >= 1 && !boundedWait(barS + 8 * ((seq - 1) % P), ((seq - 1) / P) & 1))
+                    ok = false;
+                if (!ok)
+                    continue;
+                dev::tcFenceAfter();
+                const uint32_t xs = xLane + (seq % L::kXDepth) * L::kXSlotBytes;
+                // This warp's half: panels 4 * half .. 4 * half + 3 into A columns 32 * half ..
+                // 32 * half + 31, two panels (16 columns) per store to keep few registers live.
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    uint32_t lo[8], hi[8];
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int p = 2 * k + i;
+                        const uint32_t wa = dev::ldsU32(xs + 256 * p) ^ 0x80808080u;
+                        const uint32_t wb = dev::ldsU32(xs + 256 * p + 128) ^ 0x80808080u;
+                        dev::int8PairToFloat<0>(wa, wb, lo[4 * i + 0], lo[4 * i + 1]);
+                        dev::int8PairToFloat<1>(wa, wb, lo[4 * i + 2], lo[4 * i + 3]);
+                        dev::int8PairToFloat<2>(wa, wb, hi[4 * i + 0], hi[4 * i + 1]);
+                        dev::int8PairToFloat<3>(wa, wb, hi[4 * i + 2], hi[4 * i + 3]);
+                    }
+                    dev::tcStore16x256bx2(aTmem + 32 * half + 16 * k, lo);
+                    dev::tcStore16x256bx2(aTmem + 32 * half + 16 * k + (16u << 16), hi);
+                }
+                dev::tcWaitSt();
+                dev::tcFenceBefore();
+                __syncwarp();
+                if (lane == 0)
+                    dev::mbarArrive(barA);
+            }
+            // ---- epilogue of this window ----
+            const uint32_t rowBase = task.sw * 32;
+            const bool split = task.partial != kNoPartial;
+            const bool haveWs = !split || (partials != nullptr && counters != nullptr);
+            if (!haveWs && threadIdx.x == 0)
+                atomicOr(&gDeviceStatus, 2u);
+            bool loaded = false;
+            if (panelCount > 0) {
+                if (ok && !boundedWait(barD, windows & 1))
+                    ok = false;
+                ++windows;
+                loaded = ok;
+                if (loaded)
+                    dev::tcFenceAfter();
+            }
+            {
+                uint32_t h[16], l[16];
+                if (loaded) {
+                    dev::tcLoad32x32bx16(dTmem + 16 * half, h);
+                    dev::tcLoad32x32bx16(dTmem + 32 + 16 * half, l);
+                    dev::tcWaitLd();
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        h[j] = l[j] = 0u;
+                }
+                if (haveWs) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int row = 16 * half + j;
+                        const float y = __uint_as_float(h[j]) + __uint_as_float(l[j]);
+                        if (!split) {
+                            if (rowBase + row < rows)
+                                __stcs(output + uint64_t(rowBase + row) * F + feature, y);
+                        } else if (task.mask & (1u << (row >> 3))) {
+                            const uint64_t block = task.partial + __popc(task.mask & ((1u << (row >> 3)) - 1));
+                            __stcg(partials + (block * 8 + (row & 7)) * F + feature, y);
+                        }
+                    }
+                }
+            }
+            if (panelCount > 0) {
+                if (loaded)
+                    dev::tcFenceBefore();
+                __syncwarp();
+                if (lane == 0)
+                    dev::mbarArrive(barR);
+            }
+            if (!split || !haveWs)
+                continue;
+            // Last-arriver merge among the consumer warps (reference src/kernel/spmm_kernel.cuh:250-282).
+            __threadfence();
+            namedBarrier(1, 32 * L::kConsumers);
+            if (threadIdx.x == 0 && ok) {
+                const uint32_t ticket =
+                    dev::ticketIncrement(counters + uint64_t(task.sw) * (F / 128), task.chunks - 1);
+                flags[0] = ticket == task.chunks - 1 ? 1u : 0u;
+            }
+            namedBarrier(1, 32 * L::kConsumers);
+            const bool last = ok && flags[0] != 0;
+            if (last) {
+                __threadfence();
+                constexpr uint32_t kVec = F / 4;
+                for (uint32_t rw = 0; rw < 4; ++rw) {
+                    const uint32_t row0 = rowBase + 8 * rw;
+                    if (row0 >= rows)
+                        break;
+                    const tcc_sw32_reduce_range red = matrix.reductions[task.reduceFirst + rw];
+                    const uint32_t validRows = min(8u, rows - row0);
+                    for (uint32_t e = threadIdx.x; e < validRows * kVec; e += 32 * L::kConsumers) {
+                        const uint32_t r = e / kVec, vv = e % kVec;
+                        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (uint32_t item = red.begin; item < red.end; ++item) {
+                            const uint64_t blk = matrix.partialIds[item];
+                            const float4 p = __ldcg(reinterpret_cast<const float4*>(partials + (blk * 8 + r) * F) + vv);
+                            sum.x += p.x;
+                            sum.y += p.y;
+                            sum.z += p.z;
+                            sum.w += p.w;
+                        }
+                        __stcs(reinterpret_cast<float4*>(output + uint64_t(row0 + r) * F) + vv, sum);
+                    }
+                }
+            }
+            namedBarrier(1, 32 * L::kConsumers); // flags[0] is reused by the next split task
+        }
+        dev::cpAsyncWaitAll();
+        if (!ok)
+            flags[1] = 1;
+    }
+    dev::tcFenceBefore();
+    __syncthreads();
+    dev::tcFenceAfter();
+    if (warp == L::kMmaWarp)
+        dev::tmemDealloc(tmem, L::kTmemCols);
+}
+
+} // namespace
+} // namespace tcc
