@@ -100,10 +100,6 @@ __device__ __forceinline__ void mbarInit(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbarArrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void mbarExpectTx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
 __device__ __forceinline__ bool mbarTryWait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile("{\n\t.reg .pred p;\n\t"
