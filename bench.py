@@ -50,6 +50,9 @@ def parse_args():
     p.add_argument("--impl", default="tcc", choices=["tcc", "reference"])
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-slices", type=int, default=8, help="window-aligned task slices per end-to-end step")
+    p.add_argument("--e2e-x-allgather", action="store_true",
+                   help="end to end on N > 1 ranks: each rank copies 1/N of packed X and the scales from the "
+                        "host and an NCCL all-gather completes them (not yet run on GPUs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-gpu-format", action="store_true", help="skip timing the GPU SW32 construction")
     p.add_argument("--no-assembly", action="store_true", help="skip the optional Y assembly across ranks")
@@ -196,7 +199,17 @@ def run_e2e(args, T, fmt, dm, lo, hi, packed, scales, F, device, stream, barrier
     packed_h = packed.cpu().pin_memory()
     scales_h = scales.cpu().pin_memory()
     y_h = torch.empty((max(0, r1 - r0), F), dtype=torch.float32).pin_memory()
-    inputs = [(packed, scales), (torch.empty_like(packed), torch.empty_like(scales))]
+    gather = args.e2e_x_allgather and world > 1
+    if gather:
+        # Inputs padded to equal shards; this rank copies its shard from the host and the
+        # all-gathers fill in the rest over NVLink (shards.gather_inputs).
+        from tcc_spmm_b200 import shards
+
+        padded, x0, x1 = shards.input_shard(fmt.cols, world, dist.get_rank())
+        inputs = [(torch.empty(padded * F, dtype=torch.int8, device=device),
+                   torch.empty(padded, dtype=torch.float32, device=device)) for _ in range(2)]
+    else:
+        inputs = [(packed, scales), (torch.empty_like(packed), torch.empty_like(scales))]
     ys = [torch.empty((fmt.rows, F), dtype=torch.float32, device=device) for _ in range(2)]
     ws = dm.workspace()
     h2d = torch.cuda.Stream(device)
@@ -216,8 +229,13 @@ def run_e2e(args, T, fmt, dm, lo, hi, packed, scales, F, device, stream, barrier
                 if i >= 2:
                     h2d.wait_event(in_free[b])
                 with torch.cuda.stream(h2d):
-                    inputs[b][0].copy_(packed_h, non_blocking=True)
-                    inputs[b][1].copy_(scales_h, non_blocking=True)
+                    if gather:
+                        # The collectives run after the shard copies on this stream, and the
+                        # stream waits for them before recording in_ready.
+                        shards.gather_inputs(inputs[b][0], inputs[b][1], packed_h, scales_h, F, non_blocking=True)
+                    else:
+                        inputs[b][0].copy_(packed_h, non_blocking=True)
+                        inputs[b][1].copy_(scales_h, non_blocking=True)
                 in_ready[b].record(h2d)
             if i == 0:
                 continue
@@ -253,7 +271,8 @@ def run_e2e(args, T, fmt, dm, lo, hi, packed, scales, F, device, stream, barrier
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     step_ms = float(ms.item()) / args.steps
     return {"value": nnz_total * F / (step_ms / 1e3), "unit": "nnz*F/s", "ms_per_step": round(step_ms, 4),
-            "h2d_bytes_per_step": int(packed.numel() + 4 * scales.numel()), "d2h_bytes_per_step": int(4 * (r1 - r0) * F),
+            "h2d_bytes_per_step": int((x1 - x0) * (F + 4)) if gather else int(packed.numel() + 4 * scales.numel()),
+            "d2h_bytes_per_step": int(4 * (r1 - r0) * F), "x_allgather": gather,
             "slices_per_step": len(slices), "gpu_launches": len(slices) * args.steps,
             "api": "tcc_launch_spmm_int8 (C ABI) via tcc_spmm_b200: DeviceMatrix.view slices, pinned host buffers, "
                    "copy streams (inputs and Y double-buffered)"}

@@ -69,4 +69,36 @@ def received_bytes(ranges: Sequence[tuple], rank: int, features: int) -> int:
     return int(sum(4 * features * (e - b) for r, (b, e) in enumerate(ranges) if r != rank))
 
 
-__all__ = ["owned_rows", "check_cover", "assemble_rows", "received_bytes"]
+def input_shard(cols: int, world: int, rank: int) -> tuple:
+    """Rows of packed X (and scales) that `rank` copies from the host when the inputs are split
+    over `world` ranks and completed by an all-gather: equal shards of the rows padded to a
+    multiple of `world` (the all-gather needs equal sizes). Returns (padded rows, first, last);
+    rows at or past `cols` are padding, read by no kernel."""
+    per = -(-cols // world)
+    return per * world, min(cols, rank * per), min(cols, (rank + 1) * per)
+
+
+def gather_inputs(packed, scales, packed_h, scales_h, features: int, group=None, non_blocking: bool = False) -> int:
+    """Give every rank the whole packed X and scales while each copies only its shard from the
+    host: rank r copies rows input_shard(...)[1:] of `packed_h` / `scales_h` (host arrays of
+    cols rows) into `packed` / `scales` (this rank's buffers of padded rows), then in-place
+    all-gathers fill in the other ranks' shards (NCCL over NVLink on GPUs, gloo on CPU). Every
+    rank must call this with the same sizes. Returns the bytes this rank copied from the host."""
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    cols = scales_h.numel()
+    padded, first, last = input_shard(cols, world, rank)
+    if packed.numel() != padded * features or scales.numel() != padded:
+        raise ValueError("input buffers must hold the padded rows")
+    per = padded // world
+    if last > first:
+        packed[first * features:last * features].copy_(packed_h[first * features:last * features],
+                                                       non_blocking=non_blocking)
+        scales[first:last].copy_(scales_h[first:last], non_blocking=non_blocking)
+    dist.all_gather_into_tensor(packed, packed[rank * per * features:(rank + 1) * per * features], group=group)
+    dist.all_gather_into_tensor(scales, scales[rank * per:(rank + 1) * per], group=group)
+    return (last - first) * (features + 4)
+
+
+__all__ = ["owned_rows", "check_cover", "assemble_rows", "received_bytes", "input_shard", "gather_inputs"]

@@ -49,3 +49,17 @@ def test_traffic_entry_matches_launch_shape():
     assert bench.profile_traffic("powerlaw128", "default", "balanced", other) is None
     assert bench.profile_traffic("powerlaw128", "default", "format") is None
     assert bench.profile_traffic("powerlaw128", "generic", "balanced") is None
+
+
+@pytest.mark.parametrize("cols,world", [(1, 2), (7, 2), (8, 4), (2_449_029, 4), (5, 8), (100, 3)])
+def test_x_shards_tile_the_rows(cols, world):
+    from tcc_spmm_b200 import shards
+
+    padded, _, _ = shards.input_shard(cols, world, 0)
+    assert padded % world == 0 and padded >= cols and padded - cols < world
+    covered = []
+    for r in range(world):
+        p, a, b = shards.input_shard(cols, world, r)
+        assert p == padded and 0 <= a <= b <= cols
+        covered.extend(range(a, b))
+    assert covered == list(range(cols))

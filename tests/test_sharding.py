@@ -1,8 +1,9 @@
 """Multi-GPU sharding logic on CPU ranks (gloo, world size 2): contiguous task ranges cut at
 window boundaries, every window owned by exactly one rank, the union of the ranks' rows equal
 to the single-rank result, the assembly of Y (one broadcast per owner range) giving every rank
-the full result, and a rank that dies surfacing as an error on the other rank within the
-process-group timeout (no GPU is involved)."""
+the full result, the end-to-end inputs copied in shards and all-gathered, and a rank that dies
+surfacing as an error on the other rank within the process-group timeout (no GPU is
+involved)."""
 from __future__ import annotations
 
 import os
@@ -121,6 +122,33 @@ def _failure_worker(rank: int, world: int, port: int, outdir: str) -> None:
         Path(outdir, "error").write_text(type(exc).__name__)
 
 
+def _inputs_worker(rank: int, world: int, port: int, outdir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    from tcc_spmm_b200 import shards
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    ok = True
+    for cols, features in ((7, 16), (64, 128), (1, 16)):
+        rng = np.random.default_rng(cols)
+        packed_h = torch.from_numpy(rng.integers(-127, 128, size=cols * features, dtype=np.int8))
+        scales_h = torch.from_numpy(rng.random(cols).astype(np.float32))
+        padded, first, last = shards.input_shard(cols, world, rank)
+        packed = torch.full((padded * features,), 85, dtype=torch.int8)   # stale contents
+        scales = torch.full((padded,), float("nan"), dtype=torch.float32)
+        copied = shards.gather_inputs(packed, scales, packed_h, scales_h, features)
+        ok &= copied == (last - first) * (features + 4)
+        ok &= torch.equal(packed[:cols * features], packed_h) and torch.equal(scales[:cols], scales_h)
+    if ok:
+        Path(outdir, f"ok{rank}").write_text("ok")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _spawn(fn, world: int):
     import torch.multiprocessing as mp
 
@@ -143,6 +171,11 @@ def test_lost_rank_is_reported_not_hung():
 
 def test_two_rank_y_assembly_gives_every_rank_the_full_result():
     out = _spawn(_assembly_worker, 2)
+    assert out.get("ok0") == "ok" and out.get("ok1") == "ok"
+
+
+def test_two_rank_input_shards_gather_to_the_full_inputs():
+    out = _spawn(_inputs_worker, 2)
     assert out.get("ok0") == "ok" and out.get("ok1") == "ok"
 
 
