@@ -11,7 +11,7 @@
 // rows, converts the half's 4 panels into A columns 32h..32h+31, and writes rows 16h..16h+15
 // of the window in the epilogue. P = 3 producer warps share the B builds (chunk c's MMA commit
 // goes to sFree[c % P]), so the producers keep pace with the faster consumers. A CTA has 12
-// warps and 3 CTAs share an SM (at most 56 registers per thread); F = 128 only.
+// warps and 3 CTAs share an SM (at most 56 registers per thread, no spills); F = 128 only.
 //
 // Not yet run on a GPU.
 #pragma once
@@ -359,14 +359,27 @@ __global__ void __launch_bounds__(Tmem8W<F, P>::kThreads, Tmem8W<F, P>::kCtasPer
         for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
             ok = gatherHalf8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, q, half, ok);
         uint32_t seq = 0, windows = 0;
-        tcc_sw32_task nextTask{};
-        if (blockIdx.x < matrix.taskCount)
-            nextTask = matrix.tasks[blockIdx.x];
+        uint32_t nextBegin = 0, nextEnd = 0;
+        if (blockIdx.x < matrix.taskCount) {
+            nextBegin = matrix.tasks[blockIdx.x].begin;
+            nextEnd = matrix.tasks[blockIdx.x].end;
+        }
         for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
-            const tcc_sw32_task task = nextTask;
-            if (tk + gridDim.x < matrix.taskCount)
-                nextTask = matrix.tasks[tk + gridDim.x];
-            const uint32_t panelCount = task.end - task.begin;
+            const uint32_t panelCount = nextEnd - nextBegin;
+            // The fields first read at the window's end are loaded now, their latency hidden by
+            // the chunks; only the next task's panel range is held a task ahead (register budget).
+            struct {
+                uint32_t sw, partial, mask, reduceFirst, chunks;
+            } task;
+            task.sw = matrix.tasks[tk].sw;
+            task.partial = matrix.tasks[tk].partial;
+            task.mask = matrix.tasks[tk].mask;
+            task.reduceFirst = matrix.tasks[tk].reduceFirst;
+            task.chunks = matrix.tasks[tk].chunks;
+            if (tk + gridDim.x < matrix.taskCount) {
+                nextBegin = matrix.tasks[tk + gridDim.x].begin;
+                nextEnd = matrix.tasks[tk + gridDim.x].end;
+            }
             const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
                 ok = gatherHalf8<F, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, q,
