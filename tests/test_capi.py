@@ -62,6 +62,20 @@ def test_errors_before_any_device_work(native):
         T.workspace_size(100, 1, 96)
 
 
+def test_kernel_variant_checks_before_any_device_work(native):
+    view = N.Sw32DeviceView()
+    view.taskCount = 1
+    launch = native.tcc_launch_spmm_int8_variant
+    assert launch(C.byref(view), 16, 16, 16, 1, 1, 128, None, None, None, 14) == 1
+    assert b"unknown SpMM kernel variant" in native.tcc_last_error()
+    assert launch(C.byref(view), 16, 16, 16, 1, 1, 128, None, None, None, -1) == 1
+    # variant 13 (two consumer warps per lane quarter) exists for 128 features only
+    assert launch(C.byref(view), 16, 16, 16, 1, 1, 256, None, None, None, 13) == 1
+    assert b"128 features" in native.tcc_last_error()
+    with pytest.raises(T.InvalidArgument):
+        T.launch_spmm_int8(view, 16, 16, 16, 1, 1, 256, stream=0, variant="tmem8w")
+
+
 def test_version_string(native):
     assert b"sm_100a" in native.tcc_version()
 
