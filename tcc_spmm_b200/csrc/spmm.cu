@@ -176,7 +176,7 @@ void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* sca
 // 6/7 = with four producer warps, 8..11 = tensor-memory kernel with (stages, producer warps)
 // (2, 1), (2, 2), (4, 2), (4, 4), 12 = tensor-memory kernel with 8-panel chunks, one stage and
 // two producer warps, 13 = the same with two consumer warps per TMEM lane quarter and three
-// producer warps (F = 128 only; checked by the caller).
+// producer warps (F = 128 only).
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
@@ -214,6 +214,8 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
     } else if (variant == 13) {
         if constexpr (F == 128)
             launchTmem8W<F, 3>(m, x, scales, y, rows, cols, partials, counters, stream);
+        else
+            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
     } else {
         launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
