@@ -151,3 +151,20 @@ def test_canonical_csr_errors_match(what):
     with pytest.raises(T.InvalidArgument) as my_err:
         T.make_canonical_csr(rows, cols, ro, si, va)
     assert str(my_err.value) == str(ref_err.value)
+
+
+def test_random_shapes_byte_identical():
+    """Randomised shapes, degrees, locality and both bucket modes against the reference builder:
+    ragged last windows (rows not a multiple of 32), few or many columns, empty rows, and
+    windows dense enough to split into several tasks."""
+    rng = np.random.default_rng(2024)
+    for trial in range(40):
+        rows = int(rng.integers(1, 400))
+        cols = int(rng.choice([1, 3, 31, 33, 257, 4096, 1 << 16]))
+        degree = float(rng.choice([0.0, 0.5, 2.0, 9.0, 40.0, 200.0]))
+        # neighbours near the row index only where the columns reach that far
+        local = float(rng.choice([0.0, 0.5, 0.95])) if cols >= rows else 0.0
+        csr = random_csr(rows, cols, degree, 100 + trial, local=local, radius=int(rng.choice([4, 64, 4096])))
+        for bucketed in (True, False):
+            mine, ref = convert_both(csr, bucketed=bucketed, threads=int(rng.choice([1, 4])))
+            assert_same_format(mine, ref)
