@@ -59,9 +59,7 @@ def parse_args():
     p.add_argument("--natural-order", action="store_true",
                    help="launch the tasks in format order instead of the balanced order (tcc_balance_tasks)")
     p.add_argument("--variant", default="default",
-                   choices=["default", "generic", "persistent32", "persistent64", "persistent32x2", "persistent64x2",
-                            "persistent32x4", "persistent64x4", "tmem2p1", "tmem2p2", "tmem4p2", "tmem4p4", "tmem8",
-                            "tmem8w"],
+                   choices=["default", "generic", "persistent32", "persistent64", "tmem8"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     return p.parse_args()

@@ -37,17 +37,17 @@ typedef enum tcc_status {
     TCC_DEVICE_TIMEOUT = 5    /* a bounded device wait ran out (see tcc_device_status) */
 } tcc_status;
 
-/* Sw32Task, 7 x u32 = 28 bytes (include/format/sw32.h:36-38 in the reference). */
+/* Sw32Task, 7 x u32 = 28 bytes (include/format/sw32.h:13-15 in the reference). */
 typedef struct tcc_sw32_task {
     uint32_t sw, begin, end, partial, mask, chunks, reduceFirst;
 } tcc_sw32_task;
 
-/* Sw32ReduceRange (include/format/sw32.h:39-41). */
+/* Sw32ReduceRange (include/format/sw32.h:16-18). */
 typedef struct tcc_sw32_reduce_range {
     uint32_t begin, end;
 } tcc_sw32_reduce_range;
 
-/* Sw32DeviceView, byte-compatible (include/format/sw32.h:70-79): nine device pointers
+/* Sw32DeviceView, byte-compatible (include/format/sw32.h:47-56): nine device pointers
  * followed by the task count. */
 typedef struct tcc_sw32_device_view {
     const uint32_t* windowOffsets;
@@ -153,7 +153,7 @@ void tcc_csr_free(tcc_csr* csr);
  * errors return TCC_INTERNAL (the reference throws std::runtime_error). */
 int tcc_load_matrix_market(const char* path, uint32_t* cols, tcc_csr** out);
 
-/* SW32 host format owned by the library (reference include/format/sw32.h:45-62). */
+/* SW32 host format owned by the library (reference include/format/sw32.h:22-39). */
 typedef struct tcc_sw32_host tcc_sw32_host;
 
 typedef struct tcc_sw32_sizes {
@@ -178,7 +178,7 @@ typedef struct tcc_sw32_arrays {
     const uint32_t* partialIds;
 } tcc_sw32_arrays;
 
-/* Replaces convertCsrToSw32 (reference include/format/sw32.h:66-67,
+/* Replaces convertCsrToSw32 (reference include/format/sw32.h:43-44,
  * src/format/sw32.cpp:69-167) including buildPanelTasks (src/format/sw32.cpp:25-65).
  * Output arrays are byte-identical to the reference; the conversion runs on `threads`
  * host threads (0 = all hardware threads). */
@@ -196,7 +196,7 @@ void tcc_sw32_host_free(tcc_sw32_host* host);
 /* SW32 format built on the GPU, owned by the library (one device allocation). */
 typedef struct tcc_sw32_device tcc_sw32_device;
 
-/* convertCsrToSw32 (reference include/format/sw32.h:66-67, src/format/sw32.cpp:69-167) and
+/* convertCsrToSw32 (reference include/format/sw32.h:43-44, src/format/sw32.cpp:69-167) and
  * buildPanelTasks (src/format/sw32.cpp:25-65) on the current device, from a canonical CSR
  * whose row_offsets (rows + 1), source_ids and values (nnz each) are device pointers. The
  * arrays are byte-identical to tcc_convert_csr_to_sw32's, and invalid input gives the same

@@ -4,8 +4,9 @@
 
 1. oracle/_lib/libtcc_oracle.so: the C restatement (tcc_oracle.c), gcc, OpenMP, IEEE
    arithmetic (no fast-math, no FP contraction).
-2. When the reference tree is present (REFERENCE_DIR, default /root/reference), the reference
-   compiled from its own sources where they lie, outputs only under oracle/_ref/:
+2. When the reference tree is present, the reference compiled from its own sources where they
+   lie, outputs only under oracle/_ref/. The tree is located by the REFERENCE_DIR environment
+   variable, else by the "reference_path" entry of the repository's BASELINE.json:
      libtcc_ref_host.so        src/format/{sw32,csr,matrix_market}.cpp + ref_host_shim.cpp
      libtcc_ref_cuda_sm80.so   src/kernel/spmm.cu + src/format/{int8_quantize,pack_int8}.cu
                                + ref_cuda_shim.cu as compute_80 PTX (JIT on the B200)
@@ -16,6 +17,7 @@
 """
 from __future__ import annotations
 
+import json
 import os
 import shutil
 import subprocess
@@ -25,7 +27,21 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "_lib"
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("REFERENCE_DIR", "/root/reference"))
+
+
+def _reference_dir() -> Path | None:
+    """The reference source tree: $REFERENCE_DIR, else BASELINE.json's "reference_path"."""
+    env = os.environ.get("REFERENCE_DIR")
+    if env:
+        return Path(env)
+    try:
+        path = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+    except (OSError, ValueError):
+        return None
+    return Path(path) if path else None
+
+
+REFERENCE = _reference_dir()
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 
 
@@ -52,7 +68,7 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def reference_present() -> bool:
-    return (REFERENCE / "src" / "format" / "sw32.cpp").exists()
+    return REFERENCE is not None and (REFERENCE / "src" / "format" / "sw32.cpp").exists()
 
 
 def build_reference(force: bool = False) -> bool:

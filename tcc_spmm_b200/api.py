@@ -4,9 +4,9 @@ Reference (Shixg-cnic/tcc_spmm)            this module
 -----------------------------------------  ----------------------------------------------
 makeCanonicalCsr   include/format/csr.h:23  make_canonical_csr
 loadMatrixMarket   include/format/csr.h:18  load_matrix_market
-convertCsrToSw32   include/format/sw32.h:66 convert_csr_to_sw32 (includes buildPanelTasks);
+convertCsrToSw32   include/format/sw32.h:43 convert_csr_to_sw32 (includes buildPanelTasks);
                                             convert_csr_to_sw32_device builds it on the GPU
-Sw32HostFormat     include/format/sw32.h:45 Sw32HostFormat
+Sw32HostFormat     include/format/sw32.h:22 Sw32HostFormat
 DeviceMatrix       src/device_matrix.cuh:8  DeviceMatrix (view(), workspace())
 SpmmWorkspace      include/spmm.cuh:10      SpmmWorkspace
 launchSpmmInt8     include/spmm.cuh:21      launch_spmm_int8
@@ -151,7 +151,7 @@ REDUCE_DTYPE = np.dtype([("begin", "<u4"), ("end", "<u4")])
 
 @dataclass
 class Sw32HostFormat:
-    """Host SW32 format and task plan (reference include/format/sw32.h:45-62)."""
+    """Host SW32 format and task plan (reference include/format/sw32.h:22-39)."""
 
     rows: int
     cols: int
@@ -501,9 +501,7 @@ def _np_of(torch_dtype):
     return {torch.int32: np.int32, torch.int64: np.int64, torch.float32: np.float32}[torch_dtype]
 
 
-KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "persistent32x2": 4,
-                   "persistent64x2": 5, "persistent32x4": 6, "persistent64x4": 7, "tmem2p1": 8, "tmem2p2": 9,
-                   "tmem4p2": 10, "tmem4p4": 11, "tmem8": 12, "tmem8w": 13}
+KERNEL_VARIANTS = {"default": 0, "generic": 1, "persistent32": 2, "persistent64": 3, "tmem8": 12}
 
 
 def launch_spmm_int8(view: N.Sw32DeviceView, packed_x, scales, output, rows: int, cols: int, features: int,

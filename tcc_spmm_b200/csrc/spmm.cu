@@ -12,10 +12,6 @@
 //   spmmTmem8Kernel (spmm_tmem8.cuh): the fast path (tcgen05 MMAs, accumulators in tensor
 //     memory, 8-panel chunks), used when packedX, Y, the partials, sourceIds and
 //     sourceMetadata are 16-byte aligned (always true for cudaMalloc'd buffers).
-//   spmmTmemKernel (spmm_tmem.cuh): the same arithmetic with 4-panel chunks and two stages
-//     (variants 8-11).
-//   spmmTmem8WKernel (spmm_tmem8w.cuh): the 8-panel kernel with two consumer warps per TMEM
-//     lane quarter and three producer warps, F = 128 only (variant 13, experimental).
 //   spmmPersistentKernel (spmm_persistent.cuh): mma.sync with register accumulators, when
 //     only the IDs or metadata are not 16-byte aligned.
 //   spmmGenericKernel (spmm_generic.cuh): any 2-byte aligned packedX (the reference's own
@@ -25,9 +21,7 @@
 #include "common.hpp"
 #include "spmm_generic.cuh"
 #include "spmm_persistent.cuh"
-#include "spmm_tmem.cuh"
 #include "spmm_tmem8.cuh"
-#include "spmm_tmem8w.cuh"
 
 #include <algorithm>
 #include <cuda_runtime.h>
@@ -38,6 +32,7 @@ namespace tcc {
 namespace {
 
 constexpr int kDefaultVariant = 12; // spmmTmem8Kernel<F, 2>
+bool knownVariant(int v) { return v == 0 || v == 1 || v == 2 || v == 3 || v == 12; }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -128,14 +123,8 @@ template <typename L, auto Kernel> LaunchShape tmemShapeOf(int device) {
     return shape[device];
 }
 
-template <int F, int STAGES, int P> LaunchShape tmemShape(int device) {
-    return tmemShapeOf<Tmem<F, STAGES, P>, spmmTmemKernel<F, STAGES, P>>(device);
-}
 template <int F, int P> LaunchShape tmem8Shape(int device) {
     return tmemShapeOf<Tmem8<F, P>, spmmTmem8Kernel<F, P>>(device);
-}
-template <int F, int P> LaunchShape tmem8wShape(int device) {
-    return tmemShapeOf<Tmem8W<F, P>, spmmTmem8WKernel<F, P>>(device);
 }
 
 template <int F, int P>
@@ -149,34 +138,8 @@ void launchTmem8(const tcc_sw32_device_view& m, const int8_t* x, const float* sc
                                                                            counters);
 }
 
-template <int F, int P>
-void launchTmem8W(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
-                  uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
-    int device = 0;
-    throwIf(cudaGetDevice(&device));
-    const LaunchShape s = tmem8wShape<F, P>(device);
-    const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
-    spmmTmem8WKernel<F, P><<<grid, Tmem8W<F, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols, partials,
-                                                                             counters);
-}
-
-template <int F, int STAGES, int P>
-void launchTmem(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
-                uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
-    int device = 0;
-    throwIf(cudaGetDevice(&device));
-    const LaunchShape s = tmemShape<F, STAGES, P>(device);
-    const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
-    spmmTmemKernel<F, STAGES, P><<<grid, Tmem<F, STAGES, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols,
-                                                                                         partials, counters);
-}
-
-// variant: 0 = default fast path, 1 = generic kernel, 2/3 = persistent kernel with 32/64
-// features per consumer warp and one producer warp, 4/5 = the same with two producer warps,
-// 6/7 = with four producer warps, 8..11 = tensor-memory kernel with (stages, producer warps)
-// (2, 1), (2, 2), (4, 2), (4, 4), 12 = tensor-memory kernel with 8-panel chunks, one stage and
-// two producer warps, 13 = the same with two consumer warps per TMEM lane quarter and three
-// producer warps (F = 128 only).
+// variant: 0 = default fast path (12), 1 = generic kernel, 2/3 = persistent mma.sync kernel with
+// 32/64 features per consumer warp, 12 = tensor-memory kernel with 8-panel chunks.
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
             uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
@@ -186,7 +149,7 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
     // persistent kernel runs.
     if (variant == 0)
         variant = kDefaultVariant;
-    if (variant >= 8 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16)))
+    if (variant == 12 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16)))
         variant = F == 128 ? 2 : 3;
     if (variant == 1 || !fast) {
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,
@@ -195,27 +158,6 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
         launchPersistent<F, 32, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else if (variant == 3) {
         launchPersistent<F, 64, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 4) {
-        launchPersistent<F, 32, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 5) {
-        launchPersistent<F, 64, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 6) {
-        launchPersistent<F, 32, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 7) {
-        launchPersistent<F, 64, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 8) {
-        launchTmem<F, 2, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 9) {
-        launchTmem<F, 2, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 10) {
-        launchTmem<F, 4, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 11) {
-        launchTmem<F, 4, 4>(m, x, scales, y, rows, cols, partials, counters, stream);
-    } else if (variant == 13) {
-        if constexpr (F == 128)
-            launchTmem8W<F, 3>(m, x, scales, y, rows, cols, partials, counters, stream);
-        else
-            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
     } else {
         launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
     }
@@ -315,18 +257,14 @@ int tcc_launch_spmm_int8(const tcc_sw32_device_view* matrix, const int8_t* packe
 }
 
 // Same contract as tcc_launch_spmm_int8 with an explicit kernel choice (tests and tuning; not
-// part of the public header): 0 default (= 12), 1 generic, 2-7 persistent (32/64-feature consumer
-// warps; 1, 2 or 4 producer warps), 8-11 tensor-memory with 4-panel chunks (stages, producers) =
-// (2, 1), (2, 2), (4, 2), (4, 4), 12 tensor-memory with 8-panel chunks, 13 the same with two
-// consumer warps per lane quarter and three producer warps (F = 128 only; experimental).
+// part of the public header): 0 default (= 12), 1 generic, 2/3 persistent mma.sync (32/64-feature
+// consumer warps), 12 tensor-memory with 8-panel chunks.
 int tcc_launch_spmm_int8_variant(const tcc_sw32_device_view* matrix, const int8_t* packed_x, const float* scales,
                                  float* output, uint32_t rows, uint32_t cols, uint32_t features, float* partials,
                                  uint32_t* counters, tcc_stream_t stream, int variant) {
     return tcc::guarded([&] {
-        if (variant < 0 || variant > 13)
+        if (!tcc::knownVariant(variant))
             throw std::invalid_argument("unknown SpMM kernel variant");
-        if (variant == 13 && features != 128)
-            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
         tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters,
                            reinterpret_cast<cudaStream_t>(stream), variant);
     });
@@ -342,10 +280,8 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             throw std::invalid_argument("null output");
         if (features != 128 && features != 256)
             throw std::invalid_argument("feature dimension must be 128 or 256");
-        if (variant < 0 || variant > 13)
+        if (!tcc::knownVariant(variant))
             throw std::invalid_argument("unknown SpMM kernel variant");
-        if (variant == 13 && features != 128)
-            throw std::invalid_argument("SpMM kernel variant 13 is built for 128 features");
         int device = 0, sms = 1;
         tcc::throwIf(cudaGetDevice(&device));
         tcc::throwIf(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
@@ -371,22 +307,13 @@ int tcc_spmm_launch_shape(uint32_t features, int variant, uint32_t* grid, uint32
             switch (variant) {
             case 2: persistent(tcc::Persist<128, 32, 1>{}, tcc::persistentGrid<128, 32, 1>(device)); break;
             case 3: persistent(tcc::Persist<128, 64, 1>{}, tcc::persistentGrid<128, 64, 1>(device)); break;
-            case 8: tmem(tcc::Tmem<128, 2, 1>{}, tcc::tmemShape<128, 2, 1>(device)); break;
-            case 9: tmem(tcc::Tmem<128, 2, 2>{}, tcc::tmemShape<128, 2, 2>(device)); break;
-            case 10: tmem(tcc::Tmem<128, 4, 2>{}, tcc::tmemShape<128, 4, 2>(device)); break;
-            case 11: tmem(tcc::Tmem<128, 4, 4>{}, tcc::tmemShape<128, 4, 4>(device)); break;
             case 12: tmem(tcc::Tmem8<128, 2>{}, tcc::tmem8Shape<128, 2>(device)); break;
-            case 13: tmem(tcc::Tmem8W<128, 3>{}, tcc::tmem8wShape<128, 3>(device)); break;
             default: break;
             }
         } else {
             switch (variant) {
             case 2: persistent(tcc::Persist<256, 32, 1>{}, tcc::persistentGrid<256, 32, 1>(device)); break;
             case 3: persistent(tcc::Persist<256, 64, 1>{}, tcc::persistentGrid<256, 64, 1>(device)); break;
-            case 8: tmem(tcc::Tmem<256, 2, 1>{}, tcc::tmemShape<256, 2, 1>(device)); break;
-            case 9: tmem(tcc::Tmem<256, 2, 2>{}, tcc::tmemShape<256, 2, 2>(device)); break;
-            case 10: tmem(tcc::Tmem<256, 4, 2>{}, tcc::tmemShape<256, 4, 2>(device)); break;
-            case 11: tmem(tcc::Tmem<256, 4, 4>{}, tcc::tmemShape<256, 4, 4>(device)); break;
             case 12: tmem(tcc::Tmem8<256, 2>{}, tcc::tmem8Shape<256, 2>(device)); break;
             default: break;
             }

@@ -1,20 +1,32 @@
-// Tensor-memory SpMM kernel with 8-panel chunks and one tensor-memory stage (tcgen05, sm_100a).
+// Tensor-memory SpMM kernel (tcgen05, sm_100a): the fast path of launchSpmmInt8.
 //
-// Same arithmetic, roles and hand-offs as spmm_tmem.cuh (see there): per panel and 128-feature
-// slice one tcgen05.mma.kind::tf32 D[128 x 64] += A[128 x 8] * B[8 x 64], A the exact INT8
-// feature values in tensor memory, B the panel's values times the source scales as a TF32
-// hi/lo pair, D the window's accumulator, Y row j = D[:, j] + D[:, 32 + j].
+// Per panel (8 source slots x the 32 rows of a window) and 128-feature slice one thread issues
+//     tcgen05.mma.cta_group::1.kind::tf32  D[128 features x 64] += A[128 x 8 sources] * B[8 x 64]
+// with
+//   A  the INT8 feature bytes of the 8 source rows as exact floats (X^T; every int8 is a TF32
+//      value), written straight into tensor memory by the consumer warps (tcgen05.st);
+//   B  the panel's values with the per-source scale folded in, b = tf32(a) * scale, as a dense
+//      K-major tile in shared memory: columns 0-31 hold tf32(b) and columns 32-63 the TF32
+//      remainder tf32(b - tf32(b)), so hi + lo carries b to 22 significant bits. A producer warp
+//      builds it (zero fill plus a scatter of the panel's nonzeros);
+//   D  the window's FP32 accumulator in tensor memory; Y row j = D[:, j] + D[:, 32 + j].
+// Every product the tensor core forms is exact, so each term is q * tf32(a) * scale to 22 bits:
+// within 2^-11 relative of the reference's tf32_rna(a) * tf32_rna(float(q) * scale)
+// (src/kernel/spmm_kernel.cuh:7-19,45-57), half its stated bound; the scale multiply moves
+// from the 1024 feature values of a panel to its few nonzeros.
 //
-// What differs is the unit of the pipeline. A chunk here is 8 panels (64 source slots) instead
-// of 4, so every per-chunk cost of the pipeline (waits and arrivals, ring bookkeeping, the ID,
-// metadata, scale and value staging, the loop) is paid once per 8 panels. In spmm_tmem.cuh those
-// costs are about two thirds of the instructions. Tensor memory holds one A stage of 64 columns
-// and the 64-column accumulator (128 columns, 4 CTAs per SM at F = 128), and shared memory one
-// buffer of B tiles, so the stage is refilled only after the MMAs of chunk c are complete. The
-// producer (B tiles) and the consumers (A columns) then refill it at the same time, both
-// waiting on that commit, and the MMA thread waits for both. The other CTAs of the SM fill the
-// gap. Power-law F128: 6.53 ms against 7.47 for spmm_tmem.cuh. With the consumers instead
-// chained behind the producer's B build, as in spmm_tmem.cuh, this kernel took 7.55 ms.
+// The kernel is persistent: CTA b of a grid of G takes tasks b, b+G, b+2G, ... and the chunks
+// (8 panels = 64 source slots) of those tasks form one stream. Tensor memory holds one A stage
+// of 64 columns and the 64-column accumulator (128 columns, 4 CTAs per SM at F = 128), shared
+// memory one buffer of B tiles, so the stage is refilled only after the MMAs of chunk c are
+// complete. The producer (B tiles) and the consumers (A columns) then refill it at the same
+// time, both waiting on that commit, and the MMA thread waits for both. The other CTAs of the
+// SM fill the gap.
+//
+// Feature order inside a consumer's TMEM lane quarter: lane l holds feature
+//     16 * (g / 4) + 2 * (g % 4) + {0, 8, 1, 9}[l / 8],   g = l % 8,
+// which lets thread t fill its lanes from ONE 32-bit word (packed16 bytes 4(t/4)..4(t/4)+3) of
+// each of two source rows. The epilogue undoes it (one 128-byte row segment per store).
 //
 // Roles (chunks of the CTA's tasks b, b+G, ... form one stream; producer pw owns chunks pw,
 // pw+P, ...):
@@ -37,12 +49,31 @@
 // from one shared dummy address per invalid slot made every SM queue on that one address (5%
 // slower on power-law F128; for the scales 2%), and a full copy of a dummy row 60%.
 #pragma once
-#include "spmm_tmem.cuh"
+#include "spmm_persistent.cuh"
 
 namespace tcc {
 namespace {
 
 constexpr int kChunk8 = 8; // panels per chunk: 64 source slots, two per producer lane
+
+// Instruction descriptor of the MMA: D FP32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 =
+// 2), both K-major, N = 64 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16).
+constexpr uint32_t kIdescTf32M128N64 =
+    (1u << 4) | (2u << 7) | (2u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+
+// Shared-memory matrix descriptor of one B tile (no swizzle, K-major core matrices of 8 rows
+// x 16 bytes): start address >> 4, leading (K) byte offset 128 >> 4, stride (8-row group) byte
+// offset 256 >> 4, descriptor version 1 (bits 46-47).
+__device__ __forceinline__ unsigned long long bTileDesc(uint32_t smemAddr) {
+    return static_cast<unsigned long long>((smemAddr >> 4) & 0x3FFFu) | (static_cast<unsigned long long>(128 >> 4) << 16) |
+           (static_cast<unsigned long long>(256 >> 4) << 32) | (1ull << 46);
+}
+
+// TMEM lane (0..31 within a consumer's quarter) -> feature within the consumer's 32.
+__device__ __forceinline__ int tmemLaneFeature(int l) {
+    const int g = l & 7, part = l >> 3;
+    return 16 * (g >> 2) + 2 * (g & 3) + ((part & 1) << 3) + (part >> 1);
+}
 
 template <int F, int P> struct Tmem8 {
     static constexpr int kSlices = F / 128;
@@ -88,7 +119,7 @@ template <int F, int P> struct Tmem8 {
     static_assert(P == 1 || P == 2, "sFree[c % 2] gives each producer consecutive phases only for P <= 2");
     static_assert(kASlotBytes % 16 == 0 && kXOff % 16 == 0 && kAOff % 16 == 0 && kVOff % 16 == 0 && kBarOff % 8 == 0,
                   "alignment");
-    static constexpr uint32_t kIdesc = Tmem<F, 2, 2>::kIdesc;
+    static constexpr uint32_t kIdesc = kIdescTf32M128N64;
 };
 
 // Position of row r (0..63) of a chunk in the consumer's X slot: within each panel (8 rows) the

@@ -69,11 +69,9 @@ def test_kernel_variant_checks_before_any_device_work(native):
     assert launch(C.byref(view), 16, 16, 16, 1, 1, 128, None, None, None, 14) == 1
     assert b"unknown SpMM kernel variant" in native.tcc_last_error()
     assert launch(C.byref(view), 16, 16, 16, 1, 1, 128, None, None, None, -1) == 1
-    # variant 13 (two consumer warps per lane quarter) exists for 128 features only
-    assert launch(C.byref(view), 16, 16, 16, 1, 1, 256, None, None, None, 13) == 1
-    assert b"128 features" in native.tcc_last_error()
-    with pytest.raises(T.InvalidArgument):
-        T.launch_spmm_int8(view, 16, 16, 16, 1, 1, 256, stream=0, variant="tmem8w")
+    for removed in (4, 8, 11, 13):  # tuning variants that lost their measurements are not built
+        assert launch(C.byref(view), 16, 16, 16, 1, 1, 128, None, None, None, removed) == 1
+        assert b"unknown SpMM kernel variant" in native.tcc_last_error()
 
 
 def test_version_string(native):

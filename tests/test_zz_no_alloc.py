@@ -43,7 +43,9 @@ def test_static_workspace_matches_caller_workspace(name, features):
         torch.cuda.synchronize()
         got = y.cpu().numpy()
         assert np.isfinite(got).all()
-        assert_within_tf32_bound(got, y_ref.cpu().numpy(), 2 * bound, f"{name}/F{features} vs caller workspace")
+        # Same kernel, inputs and merge order as the caller-workspace call: the bits must match.
+        assert np.array_equal(got.view(np.uint32), y_ref.cpu().numpy().view(np.uint32)), \
+            f"{name}/F{features}: static workspace differs from caller workspace"
         assert_within_tf32_bound(got, oracle, bound, f"{name}/F{features} vs oracle")
     assert T.device_status() == 0
 
