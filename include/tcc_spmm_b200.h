@@ -114,18 +114,26 @@ int tcc_spmm_workspace_size(uint32_t rows, uint32_t partial_count, uint32_t feat
  * counters live in a static device scratch of this library (8 MiB of partials, i.e.
  * partial_count * 8 * features <= 2^21 floats, and 1 MiB of counters, i.e.
  * ceil(rows / 32) * features / 128 <= 2^18 words); larger needs return
- * TCC_INVALID_ARGUMENT. The library allocates nothing: the first call on a device looks up
- * the scratch's address (do it before any stream capture). The counters start at zero and
- * every completed call leaves them at zero. Calls on one device share the scratch, so they
- * must not overlap (serialise them on one stream). No counterpart in the reference, whose
- * launchSpmmInt8 always takes the caller's SpmmWorkspace (include/spmm.cuh:10-23). */
+ * TCC_INVALID_ARGUMENT. partial_count must be the format's partialCount: the view does not
+ * carry it, and a smaller value lets split tasks write past the checked size (undefined).
+ * The library allocates nothing: the first call on a device looks up the scratch's address
+ * (do it before any stream capture). The counters start at zero and every completed call
+ * leaves them at zero; after a call whose bounded wait ran out, tcc_device_status(&s, 1)
+ * returns them to zero. Calls on one device share the scratch, so they must not overlap
+ * (serialise them on one stream). No counterpart in the reference, whose launchSpmmInt8
+ * always takes the caller's SpmmWorkspace (include/spmm.cuh:10-23). */
 int tcc_launch_spmm_int8_static_workspace(const tcc_sw32_device_view* matrix, const int8_t* packed_x,
                                           const float* scales, float* output, uint32_t rows,
                                           uint32_t cols, uint32_t features, uint32_t partial_count,
                                           tcc_stream_t stream);
 
-/* Status word written by bounded device waits of the SpMM kernel on the current device:
- * 0 = no wait ran out since the last reset. Synchronises the device. */
+/* Status word of the SpMM kernels on the current device since the last reset: bit 0 = a
+ * bounded device wait ran out (the launch returned early, Y is incomplete, and the tickets of
+ * split windows may be left short of zero), bit 1 = a split task found no partial/counter
+ * workspace (its rows were not written). Synchronises the device. reset != 0 clears the word
+ * and returns the static workspace's counters to zero; counters in a caller's workspace are
+ * the caller's to re-zero (cudaMemset) after bit 0. No counterpart in the reference, whose
+ * kernel has no bounded waits. */
 int tcc_device_status(uint32_t* status, int reset);
 
 /* ---------------------------------------------------------------------------------

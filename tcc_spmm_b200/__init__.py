@@ -8,7 +8,7 @@ reference's host API in Python for tests and benchmarks.
 from .api import (BUCKET_ORDER, NO_PARTIAL, PADDING_SOURCE, TASK_PANEL_LIMIT, CsrMatrix, CudaError, DeviceMatrix,
                   balance_tasks,
                   DeviceTimeout, InvalidArgument, MtxMatrix, SpmmWorkspace, Sw32DeviceFormat, Sw32HostFormat,
-                  convert_csr_to_sw32, convert_csr_to_sw32_device, device_status, launch_spmm_int8,
+                  check_device, convert_csr_to_sw32, convert_csr_to_sw32_device, device_status, launch_spmm_int8,
                   load_matrix_market, make_canonical_csr, pack_features_int8x16, partition_tasks,
                   quantize_features_int8, quantize_pack_features_int8, spmm_launch_shape, sw32_device_trim,
                   workspace_size)
@@ -17,7 +17,8 @@ from ._native import library_path
 __all__ = [
     "BUCKET_ORDER", "NO_PARTIAL", "PADDING_SOURCE", "TASK_PANEL_LIMIT", "CsrMatrix", "CudaError", "DeviceMatrix",
     "DeviceTimeout", "InvalidArgument", "MtxMatrix", "SpmmWorkspace", "Sw32DeviceFormat", "Sw32HostFormat",
-    "convert_csr_to_sw32", "convert_csr_to_sw32_device", "device_status", "launch_spmm_int8", "load_matrix_market",
+    "check_device", "convert_csr_to_sw32", "convert_csr_to_sw32_device", "device_status", "launch_spmm_int8",
+    "load_matrix_market",
     "make_canonical_csr", "pack_features_int8x16", "partition_tasks", "quantize_features_int8",
     "quantize_pack_features_int8", "spmm_launch_shape", "sw32_device_trim", "workspace_size",
     "library_path", "balance_tasks",

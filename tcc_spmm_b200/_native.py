@@ -120,6 +120,14 @@ SIGNATURES = {
     "tcc_sw32_device_trim": (C.c_int, []),
 }
 
+# Failure-path test hooks of the library (exported, not declared in the public header).
+TEST_SIGNATURES = {
+    "tcc_test_launch_spmm_int8_stalled": (C.c_int, [C.POINTER(Sw32DeviceView), C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p,
+                                                    C.c_uint32, C.c_int, C.c_void_p]),
+    "tcc_test_static_counters_nonzero": (C.c_int, [u64p]),
+}
+
 WL_SIGNATURES = {
     "tcc_wl_last_error": (C.c_char_p, []),
     "tcc_wl_free": (None, [C.POINTER(WlCsr)]),
@@ -154,7 +162,7 @@ def _load(path: Path, signatures: dict) -> C.CDLL:
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        _lib = _load(library_path(), SIGNATURES)
+        _lib = _load(library_path(), {**SIGNATURES, **TEST_SIGNATURES})
     return _lib
 
 

@@ -547,8 +547,28 @@ def quantize_pack_features_int8(x, packed, scale, sources: int, features: int, s
                                                    _stream_handle(stream, packed)))
 
 
+STATUS_WAIT_TIMEOUT = 1   # a bounded device wait ran out (the launch returned early)
+STATUS_NO_WORKSPACE = 2   # a split task found no partial/counter workspace
+
+
 def device_status(reset: bool = False) -> int:
-    """Status word of bounded device waits (0 = none ran out). Synchronises the device."""
+    """Status word of the SpMM kernels on the current device (0 = no failure since the last
+    reset; bits STATUS_WAIT_TIMEOUT and STATUS_NO_WORKSPACE). Synchronises the device. reset
+    also returns the static workspace's counters to zero."""
     st = C.c_uint32()
     _check(N.lib().tcc_device_status(C.byref(st), int(reset)))
     return st.value
+
+
+def check_device(reset: bool = True) -> None:
+    """Raise for a device-side failure reported since the last reset: DeviceTimeout when a
+    bounded wait ran out (Y of those launches is incomplete, and a caller-owned workspace's
+    counters must be re-zeroed), InvalidArgument when a split task was launched without a
+    partial/counter workspace (the reference contract allows a null workspace only when
+    partialCount is 0, include/spmm.cuh:8). Synchronises the device; reset clears the word."""
+    status = device_status(reset)
+    if status & STATUS_WAIT_TIMEOUT:
+        raise DeviceTimeout(f"a bounded wait of the SpMM kernel ran out (device status {status:#x})")
+    if status & STATUS_NO_WORKSPACE:
+        raise InvalidArgument("split tasks need the partial/counter workspace (partialCount > 0); "
+                              f"their rows were not written (device status {status:#x})")

@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace tcc {
 namespace {
@@ -129,20 +130,21 @@ template <int F, int P> LaunchShape tmem8Shape(int device) {
 
 template <int F, int P>
 void launchTmem8(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
-                 uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream) {
+                 uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, uint32_t testFlags) {
     int device = 0;
     throwIf(cudaGetDevice(&device));
     const LaunchShape s = tmem8Shape<F, P>(device);
     const uint32_t grid = std::min<uint32_t>(m.taskCount, s.grid);
     spmmTmem8Kernel<F, P><<<grid, Tmem8<F, P>::kThreads, s.smem, stream>>>(m, x, scales, y, rows, cols, partials,
-                                                                           counters);
+                                                                           counters, testFlags);
 }
 
 // variant: 0 = default fast path (12), 1 = generic kernel, 2/3 = persistent mma.sync kernel with
 // 32/64 features per consumer warp, 12 = tensor-memory kernel with 8-panel chunks.
 template <int F>
 void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales, float* y, uint32_t rows,
-            uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant) {
+            uint32_t cols, float* partials, uint32_t* counters, cudaStream_t stream, int variant,
+            uint32_t testFlags) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
     // Default: the tensor-memory kernel with 8-panel chunks and two producer warps. It moves
     // the IDs and metadata with bulk copies, which need 16-byte aligned arrays; otherwise the
@@ -159,14 +161,14 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
     } else if (variant == 3) {
         launchPersistent<F, 64, 1>(m, x, scales, y, rows, cols, partials, counters, stream);
     } else {
-        launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream);
+        launchTmem8<F, 2>(m, x, scales, y, rows, cols, partials, counters, stream, testFlags);
     }
     throwIf(cudaGetLastError());
 }
 
 void launchChecked(const tcc_sw32_device_view* matrix, const int8_t* packedX, const float* scales, float* output,
                    uint32_t rows, uint32_t cols, uint32_t features, float* partials, uint32_t* counters,
-                   cudaStream_t stream, int variant) {
+                   cudaStream_t stream, int variant, uint32_t testFlags = 0) {
     if (matrix == nullptr)
         throw std::invalid_argument("null SW32 device view");
     if (features != 128 && features != 256)
@@ -179,9 +181,9 @@ void launchChecked(const tcc_sw32_device_view* matrix, const int8_t* packedX, co
     if (!aligned(packedX, 2) || !aligned(output, 4))
         throw std::invalid_argument("packedX must be 2-byte and Y 4-byte aligned");
     if (features == 128)
-        launch<128>(*matrix, packedX, scales, output, rows, cols, partials, counters, stream, variant);
+        launch<128>(*matrix, packedX, scales, output, rows, cols, partials, counters, stream, variant, testFlags);
     else
-        launch<256>(*matrix, packedX, scales, output, rows, cols, partials, counters, stream, variant);
+        launch<256>(*matrix, packedX, scales, output, rows, cols, partials, counters, stream, variant, testFlags);
 }
 
 // ---- static split-window workspace (tcc_launch_spmm_int8_static_workspace) ---------------
@@ -219,6 +221,26 @@ StaticWorkspace staticWorkspace() {
     return w;
 }
 
+// The launch of tcc_launch_spmm_int8_static_workspace: sizes checked against the static scratch,
+// whose device addresses are looked up once per device.
+void launchStatic(const tcc_sw32_device_view* matrix, const int8_t* packedX, const float* scales, float* output,
+                  uint32_t rows, uint32_t cols, uint32_t features, uint32_t partialCount, cudaStream_t stream,
+                  uint32_t testFlags) {
+    if (features != 128 && features != 256)
+        throw std::invalid_argument("feature dimension must be 128 or 256");
+    const uint64_t partialFloats = uint64_t(partialCount) * 8 * features;
+    const uint64_t counterWords = partialCount ? (uint64_t(rows) + 31) / 32 * (features / 128) : 0;
+    if (partialFloats > kStaticPartialFloats)
+        throw std::invalid_argument("split-window partials need " + std::to_string(partialFloats * 4) +
+                                    " bytes; the static workspace holds " + std::to_string(kStaticPartialFloats * 4));
+    if (counterWords > kStaticCounterWords)
+        throw std::invalid_argument("split-window counters need " + std::to_string(counterWords * 4) +
+                                    " bytes; the static workspace holds " + std::to_string(kStaticCounterWords * 4));
+    const StaticWorkspace w = staticWorkspace();
+    launchChecked(matrix, packedX, scales, output, rows, cols, features, partialCount ? w.partials : nullptr,
+                  partialCount ? w.counters : nullptr, stream, 0, testFlags);
+}
+
 } // namespace
 } // namespace tcc
 
@@ -228,22 +250,8 @@ int tcc_launch_spmm_int8_static_workspace(const tcc_sw32_device_view* matrix, co
                                           const float* scales, float* output, uint32_t rows, uint32_t cols,
                                           uint32_t features, uint32_t partial_count, tcc_stream_t stream) {
     return tcc::guarded([&] {
-        if (features != 128 && features != 256)
-            throw std::invalid_argument("feature dimension must be 128 or 256");
-        const uint64_t partialFloats = uint64_t(partial_count) * 8 * features;
-        const uint64_t counterWords = partial_count ? (uint64_t(rows) + 31) / 32 * (features / 128) : 0;
-        if (partialFloats > tcc::kStaticPartialFloats)
-            throw std::invalid_argument("split-window partials need " + std::to_string(partialFloats * 4) +
-                                        " bytes; the static workspace holds " +
-                                        std::to_string(tcc::kStaticPartialFloats * 4));
-        if (counterWords > tcc::kStaticCounterWords)
-            throw std::invalid_argument("split-window counters need " + std::to_string(counterWords * 4) +
-                                        " bytes; the static workspace holds " +
-                                        std::to_string(tcc::kStaticCounterWords * 4));
-        const tcc::StaticWorkspace w = tcc::staticWorkspace();
-        tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features,
-                           partial_count ? w.partials : nullptr, partial_count ? w.counters : nullptr,
-                           reinterpret_cast<cudaStream_t>(stream), 0);
+        tcc::launchStatic(matrix, packed_x, scales, output, rows, cols, features, partial_count,
+                          reinterpret_cast<cudaStream_t>(stream), 0);
     });
 }
 
@@ -332,8 +340,57 @@ int tcc_device_status(uint32_t* status, int reset) {
             const uint32_t zero = 0;
             s = cudaMemcpyToSymbol(tcc::gDeviceStatus, &zero, sizeof(uint32_t));
         }
+        if (s == cudaSuccess && reset) {
+            // A launch whose wait ran out skips the tickets of its split windows and leaves their
+            // counters short of zero. The caller re-zeroes a workspace it owns; the static
+            // workspace's counters are re-zeroed here (the device is idle after the synchronise).
+            const tcc::StaticWorkspace w = tcc::staticWorkspace();
+            s = cudaMemset(w.counters, 0, tcc::kStaticCounterWords * sizeof(uint32_t));
+            if (s == cudaSuccess)
+                s = cudaDeviceSynchronize();
+        }
         if (s != cudaSuccess)
             throw tcc::CudaError(cudaGetErrorString(s));
+    });
+}
+
+// ---- failure-path test hooks (not part of the public header) -----------------------------
+
+// tcc_launch_spmm_int8 (static_workspace = 0, caller's partials and counters) or
+// tcc_launch_spmm_int8_static_workspace (static_workspace = 1) with the MMA thread of every odd
+// CTA of the default kernel stalled on a barrier that nothing completes: its bounded wait runs
+// out after about two seconds, the waits of that CTA's other roles run out after it, and status
+// bit 0 is set. The split windows whose tasks ran on both even and odd CTAs keep counters short
+// of zero. No wait is unbounded and no access leaves the inputs, outputs and workspace.
+int tcc_test_launch_spmm_int8_stalled(const tcc_sw32_device_view* matrix, const int8_t* packed_x,
+                                      const float* scales, float* output, uint32_t rows, uint32_t cols,
+                                      uint32_t features, float* partials, uint32_t* counters, uint32_t partial_count,
+                                      int static_workspace, tcc_stream_t stream) {
+    return tcc::guarded([&] {
+        const auto st = reinterpret_cast<cudaStream_t>(stream);
+        if (static_workspace)
+            tcc::launchStatic(matrix, packed_x, scales, output, rows, cols, features, partial_count, st,
+                              tcc::kTestStallOddCtas);
+        else
+            tcc::launchChecked(matrix, packed_x, scales, output, rows, cols, features, partials, counters, st, 12,
+                               tcc::kTestStallOddCtas);
+    });
+}
+
+// Number of nonzero words in the static workspace's counters on the current device (synchronises
+// the device).
+int tcc_test_static_counters_nonzero(uint64_t* nonzero) {
+    return tcc::guarded([&] {
+        if (nonzero == nullptr)
+            throw std::invalid_argument("null output");
+        const tcc::StaticWorkspace w = tcc::staticWorkspace();
+        std::vector<uint32_t> host(tcc::kStaticCounterWords);
+        cudaError_t s = cudaDeviceSynchronize();
+        if (s == cudaSuccess)
+            s = cudaMemcpy(host.data(), w.counters, host.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+        if (s != cudaSuccess)
+            throw tcc::CudaError(cudaGetErrorString(s));
+        *nonzero = static_cast<uint64_t>(std::count_if(host.begin(), host.end(), [](uint32_t v) { return v != 0; }));
     });
 }
 

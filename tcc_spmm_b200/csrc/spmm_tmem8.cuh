@@ -55,6 +55,7 @@ namespace tcc {
 namespace {
 
 constexpr int kChunk8 = 8; // panels per chunk: 64 source slots, two per producer lane
+constexpr uint32_t kTestStallOddCtas = 1; // testFlags bit: stall the MMA thread of odd CTAs
 
 // Instruction descriptor of the MMA: D FP32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 =
 // 2), both K-major, N = 64 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16).
@@ -167,7 +168,7 @@ template <int F, int P>
 __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPerSm)
     spmmTmem8Kernel(const tcc_sw32_device_view matrix, const int8_t* __restrict__ packedX,
                     const float* __restrict__ scales, float* __restrict__ output, uint32_t rows, uint32_t cols,
-                    float* __restrict__ partials, uint32_t* __restrict__ counters) {
+                    float* __restrict__ partials, uint32_t* __restrict__ counters, uint32_t testFlags) {
     using L = Tmem8<F, P>;
     extern __shared__ __align__(128) unsigned char smem[];
     const int warp = threadIdx.x >> 5;
@@ -350,6 +351,12 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         if (lane == 0) {
             bool ok = true, issued = false;
             uint32_t seq = 0, windows = 0;
+            // Failure-path test (kTestStallOddCtas): the MMA thread of every odd CTA first waits
+            // on the drain barrier, which nothing completes before the end, so that wait runs out
+            // and the other roles' waits for its commits run out after it. Every wait stays
+            // bounded; the CTA drains its copies, frees its tensor memory and returns.
+            if ((testFlags & kTestStallOddCtas) && (blockIdx.x & 1u))
+                ok = boundedWait(barF, 0);
             // The next task's panel range is loaded one task ahead, off the MMA issue path.
             uint32_t nextBegin = 0, nextEnd = 0;
             if (blockIdx.x < matrix.taskCount) {

@@ -74,6 +74,24 @@ def test_kernel_variant_checks_before_any_device_work(native):
         assert b"unknown SpMM kernel variant" in native.tcc_last_error()
 
 
+def test_static_workspace_checks_before_any_device_work(native):
+    """The no-allocation entry point rejects what its fixed scratch cannot hold, and a feature
+    count the kernels do not support, before it touches a device."""
+    view = N.Sw32DeviceView()
+    view.taskCount = 1
+    launch = native.tcc_launch_spmm_int8_static_workspace
+    assert launch(C.byref(view), 16, 16, 16, 1, 1, 64, 0, None) == 1
+    assert b"128 or 256" in native.tcc_last_error()
+    # counters: ceil(rows / 32) * F / 128 words; 2^18 fit, one window more does not
+    assert launch(C.byref(view), 16, 16, 16, (1 << 23) + 1, 1, 128, 1, None) == 1
+    assert b"split-window counters need" in native.tcc_last_error()
+    assert launch(C.byref(view), 16, 16, 16, (1 << 22) + 1, 1, 256, 1, None) == 1
+    assert b"split-window counters need" in native.tcc_last_error()
+    # partials: partial_count * 8 * F floats; 2^21 fit, one block more does not
+    assert launch(C.byref(view), 16, 16, 16, 64, 1, 128, (1 << 11) + 1, None) == 1
+    assert b"split-window partials need" in native.tcc_last_error()
+
+
 def test_version_string(native):
     assert b"sm_100a" in native.tcc_version()
 

@@ -61,3 +61,40 @@ def test_static_workspace_rejects_oversized_partials():
         case.fmt.cols, 128, 1 << 20, torch.cuda.current_stream().cuda_stream)
     assert status == 1  # TCC_INVALID_ARGUMENT
     assert b"static workspace" in N.lib().tcc_last_error()
+
+
+def _static_nonzero_counters() -> int:
+    n = C.c_uint64()
+    assert N.lib().tcc_test_static_counters_nonzero(C.byref(n)) == 0, N.lib().tcc_last_error()
+    return n.value
+
+
+def test_static_workspace_recovers_after_a_wait_runs_out():
+    """A launch whose bounded wait runs out leaves split-window counters short of zero. The
+    static workspace belongs to the library, so the caller cannot re-zero it: the status reset
+    (tcc_device_status with reset) does, and the next call is bit-identical to the caller-
+    workspace call again."""
+    import torch
+
+    T.device_status(reset=True)
+    case = build_case(EDGE_CASES["split_769"](), 128, seed=29)
+    y_ref = torch.full((case.fmt.rows, 128), float("nan"), device="cuda")
+    T.launch_spmm_int8(case.dm.view(), case.packed_dev, case.scales_dev, y_ref, case.fmt.rows, case.fmt.cols, 128,
+                       case.dm.workspace())
+    y = torch.full_like(y_ref, float("nan"))
+    view = case.dm.view()
+    status = N.lib().tcc_test_launch_spmm_int8_stalled(
+        C.byref(view), case.packed_dev.data_ptr(), case.scales_dev.data_ptr(), y.data_ptr(), case.fmt.rows,
+        case.fmt.cols, 128, None, None, case.fmt.partial_count, 1, torch.cuda.current_stream().cuda_stream)
+    assert status == 0, N.lib().tcc_last_error()
+    assert T.device_status() & T.api.STATUS_WAIT_TIMEOUT
+    assert _static_nonzero_counters() > 0
+    with pytest.raises(T.DeviceTimeout):
+        T.check_device(reset=True)
+    assert _static_nonzero_counters() == 0
+    for _ in range(2):
+        y = torch.full_like(y_ref, float("nan"))
+        assert _static_call(case, y) == 0, N.lib().tcc_last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32))
+    assert T.device_status() == 0
