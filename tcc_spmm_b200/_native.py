@@ -140,6 +140,11 @@ WL_SIGNATURES = {
     "tcc_wl_rmat": (C.c_int, [C.c_uint32, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_uint64, C.c_uint32,
                               C.POINTER(C.POINTER(WlCsr))]),
     "tcc_wl_normal": (C.c_int, [f32p, C.c_uint64, C.c_uint64, C.c_uint32]),
+    "tcc_wl_rmat_device": (C.c_int, [C.c_uint32, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_uint64,
+                                     C.c_void_p, C.POINTER(C.c_void_p)]),
+    "tcc_wl_device_csr_arrays": (C.c_int, [C.c_void_p, u32p, u32p, u64p, C.POINTER(C.c_void_p),
+                                           C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "tcc_wl_device_csr_free": (None, [C.c_void_p]),
 }
 
 

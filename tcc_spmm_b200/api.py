@@ -349,9 +349,13 @@ class DeviceMatrix:
                                 self.partial_ids.data_ptr(), last - first)
 
     @classmethod
-    def from_device_format(cls, fmt: "Sw32DeviceFormat", features: int) -> "DeviceMatrix":
+    def from_device_format(cls, fmt: "Sw32DeviceFormat", features: int, task_range: Optional[tuple] = None,
+                           balance: bool = False, variant: str = "default", host_tasks: Optional[np.ndarray] = None,
+                           host_masks: Optional[np.ndarray] = None) -> "DeviceMatrix":
         """A DeviceMatrix over a format built on the GPU (no upload): the arrays are the
-        library's; only the workspace for `features` is allocated here."""
+        library's; only the workspace for `features` is allocated here. task_range and balance
+        as in the constructor; balancing reads the tasks and row-group masks on the host
+        (host_tasks / host_masks when given, else copied from the device)."""
         import torch
 
         self = cls.__new__(cls)
@@ -360,7 +364,20 @@ class DeviceMatrix:
         for name in ("window_offsets", "source_ids", "row_group_masks", "source_metadata", "values",
                      "bucket_offsets", "tasks", "reductions", "partial_ids"):
             setattr(self, name, getattr(fmt, name))
-        self.task_count, self.partial_count = fmt.task_count, fmt.partial_count
+        lo, hi = (0, fmt.task_count) if task_range is None else (int(task_range[0]), int(task_range[1]))
+        if not 0 <= lo <= hi <= fmt.task_count:
+            raise ValueError("task range out of bounds")
+        words = TASK_DTYPE.itemsize // 4
+        self.tasks = fmt.tasks[words * lo:words * hi] if hi > lo else fmt.tasks[:words]
+        self.task_count, self.partial_count = hi - lo, fmt.partial_count
+        self.tasks_balanced = None
+        if balance and self.task_count:
+            tasks = host_tasks if host_tasks is not None else fmt.tasks.cpu().numpy().view(np.uint32).view(TASK_DTYPE)
+            masks = host_masks if host_masks is not None else fmt.row_group_masks.cpu().numpy().view(np.uint32)
+            with torch.cuda.device(self.device):
+                grid = spmm_launch_shape(features, variant)["grid"] or spmm_launch_shape(features)["grid"]
+            order = balance_tasks(tasks[lo:hi], masks, features, grid)
+            self.tasks_balanced = torch.from_numpy(order.view(np.uint32).view(np.int32)).to(self.device)
         self._format = fmt
         pf, cw = workspace_size(fmt.rows, fmt.partial_count, features)
         self.partials = torch.empty(pf, dtype=torch.float32, device=self.device) if pf else None
@@ -432,8 +449,8 @@ class Sw32DeviceFormat:
             reductions=h(self.reductions, np.uint32).view(REDUCE_DTYPE), partial_ids=h(self.partial_ids, np.uint32),
             partial_count=self.partial_count)
 
-    def device_matrix(self, features: int) -> "DeviceMatrix":
-        return DeviceMatrix.from_device_format(self, features)
+    def device_matrix(self, features: int, **kwargs) -> "DeviceMatrix":
+        return DeviceMatrix.from_device_format(self, features, **kwargs)
 
     def differences(self, host: Sw32HostFormat) -> list:
         """Names of the arrays (and counts) that differ from `host`, compared bit for bit on the

@@ -74,12 +74,22 @@ def build_library(force: bool = False, verbose_ptxas: bool = False) -> Path:
 
 
 def build_workloads(force: bool = False) -> Path:
-    """Compile libtcc_workloads.so (seeded synthetic matrices; host only)."""
+    """Compile libtcc_workloads.so (seeded synthetic matrices: host generators, and the R-MAT
+    generator for sm_100a devices)."""
     LIBDIR.mkdir(exist_ok=True)
-    src = CSRC / "workloads.cpp"
+    obj_dir = BUILD / "obj"
+    obj_dir.mkdir(parents=True, exist_ok=True)
+    deps = [CSRC / "workloads.h"]
+    host_src, gpu_src = CSRC / "workloads.cpp", CSRC / "workloads_gpu.cu"
+    host_obj, gpu_obj = obj_dir / "workloads.cpp.o", obj_dir / "workloads_gpu.cu.o"
+    if force or _stale(host_obj, [host_src, *deps]):
+        _run([CXX, "-O3", "-std=c++17", "-fPIC", "-pthread", "-I", str(CSRC), "-c", str(host_src), "-o", str(host_obj)])
+    if force or _stale(gpu_obj, [gpu_src, *deps]):
+        _run([NVCC, *ARCH, "-lineinfo", "-Xcompiler", "-fPIC", "-O3", "-std=c++17", "-I", str(CSRC), "-c", str(gpu_src),
+              "-o", str(gpu_obj)])
     lib = LIBDIR / "libtcc_workloads.so"
-    if force or _stale(lib, [src, CSRC / "workloads.h"]):
-        _run([CXX, "-O3", "-std=c++17", "-fPIC", "-shared", "-pthread", "-I", str(CSRC), str(src), "-o", str(lib)])
+    if force or _stale(lib, [host_obj, gpu_obj]):
+        _run([NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", str(host_obj), str(gpu_obj), "-o", str(lib), "-lpthread"])
     return lib
 
 

@@ -155,6 +155,9 @@ uint32_t poissonDraw(Stream& rng, double mean) {
 
 } // namespace
 
+// Error message of the calling thread's last failed call (shared with workloads_gpu.cu).
+void tccWlSetLastError(const char* message) { lastError = message ? message : ""; }
+
 extern "C" {
 
 const char* tcc_wl_last_error(void) { return lastError.c_str(); }

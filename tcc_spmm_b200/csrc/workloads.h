@@ -29,6 +29,19 @@ int tcc_wl_rmat(uint32_t scale, uint64_t edges, double a, double b, double c, ui
 /* count N(0,1) floats (Box-Muller). */
 int tcc_wl_normal(float* out, uint64_t count, uint64_t seed, uint32_t threads);
 
+/* The same R-MAT matrix as tcc_wl_rmat (bit for bit), generated on the current CUDA device in
+ * device memory owned by the returned handle: the edge draws of every sampling block from the
+ * same counter-based stream, a radix sort of (row, column) keys, duplicate removal, per-row
+ * degrees and 1/deg_i values. `stream` is a cudaStream_t; the call returns once the arrays are
+ * complete. Scratch of about 16 bytes per edge sample is allocated and freed inside the call. */
+typedef struct tcc_wl_device_csr tcc_wl_device_csr;
+int tcc_wl_rmat_device(uint32_t scale, uint64_t edges, double a, double b, double c, uint64_t seed, void* stream,
+                       tcc_wl_device_csr** out);
+/* Sizes and device arrays of a generated matrix (valid until tcc_wl_device_csr_free). */
+int tcc_wl_device_csr_arrays(const tcc_wl_device_csr* csr, uint32_t* rows, uint32_t* cols, uint64_t* nnz,
+                             uint32_t** row_offsets, uint32_t** source_ids, float** values);
+void tcc_wl_device_csr_free(tcc_wl_device_csr* csr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,6 +97,81 @@ def generate(name: str, threads: int = 0) -> CsrMatrix:
     return fn(*cfg.params, seed=cfg.seed, threads=threads)
 
 
+@dataclass
+class DeviceCsr:
+    """A canonical CSR in device memory (torch tensors: row_offsets int32 [rows + 1], source_ids
+    int32 [nnz], values float32 [nnz]; the int32 tensors hold the u32 arrays)."""
+
+    rows: int
+    cols: int
+    row_offsets: object
+    source_ids: object
+    values: object
+
+    @property
+    def nnz(self) -> int:
+        return int(self.values.numel())
+
+    def to_host(self) -> CsrMatrix:
+        return CsrMatrix(self.rows, self.cols, self.row_offsets.cpu().numpy().view(np.uint32),
+                         self.source_ids.cpu().numpy().view(np.uint32), self.values.cpu().numpy())
+
+
+def rmat_device(scale: int, edges: int, a: float, b: float, c: float, seed: int, device="cuda") -> DeviceCsr:
+    """tcc_wl_rmat's matrix, bit for bit, generated on `device` (tcc_wl_rmat_device). The arrays
+    are copied into torch tensors and the library's buffers freed before returning."""
+    import torch
+
+    device = torch.device(device)
+    lib = N.workloads()
+    handle = C.c_void_p()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        if lib.tcc_wl_rmat_device(scale, edges, a, b, c, seed, stream.cuda_stream, C.byref(handle)) != 0:
+            raise RuntimeError(lib.tcc_wl_last_error().decode())
+        try:
+            rows, cols, nnz = C.c_uint32(), C.c_uint32(), C.c_uint64()
+            ro, si, va = C.c_void_p(), C.c_void_p(), C.c_void_p()
+            if lib.tcc_wl_device_csr_arrays(handle, C.byref(rows), C.byref(cols), C.byref(nnz), C.byref(ro),
+                                            C.byref(si), C.byref(va)) != 0:
+                raise RuntimeError(lib.tcc_wl_last_error().decode())
+
+            def copy(ptr, count, dtype, typestr):
+                out = torch.empty(int(count), dtype=dtype, device=device)
+                if count:
+                    src = torch.as_tensor(_DeviceBuffer(ptr.value, count, typestr), device=device)
+                    out.copy_(src)
+                return out
+
+            result = DeviceCsr(rows.value, cols.value, copy(ro, rows.value + 1, torch.int32, "<i4"),
+                               copy(si, nnz.value, torch.int32, "<i4"), copy(va, nnz.value, torch.float32, "<f4"))
+            torch.cuda.current_stream(device).synchronize()
+            return result
+        finally:
+            lib.tcc_wl_device_csr_free(handle)
+
+
+class _DeviceBuffer:
+    def __init__(self, ptr: int, count: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def generate_device(name: str, device="cuda", threads: int = 0) -> DeviceCsr:
+    """The configuration's matrix in device memory: R-MAT generated on the device, the others
+    generated on the host (`threads`) and copied up. Identical to generate(name)."""
+    import torch
+
+    cfg = CONFIGS[name]
+    if cfg.kind == "rmat":
+        scale, edges, a, b, c = cfg.params
+        return rmat_device(scale, edges, a, b, c, cfg.seed, device)
+    csr = generate(name, threads=threads)
+    up = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(device)
+    return DeviceCsr(csr.rows, csr.cols, up(csr.row_offsets, np.int32), up(csr.source_ids, np.int32),
+                     up(csr.values, np.float32))
+
+
 def normal_features(rows: int, features: int, seed: int = FEATURE_SEED, threads: int = 0) -> np.ndarray:
     """rows x features float32 N(0,1), row-major."""
     out = np.empty((rows, features), dtype=np.float32)

@@ -12,29 +12,65 @@ from tcc_spmm_b200 import workloads as W
 
 
 @pytest.fixture(scope="module")
-def fmt():
+def case():
     csr = W.generate("stress_small")
-    return T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+    return csr, T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+
+
+@pytest.fixture(scope="module")
+def fmt(case):
+    return case[1]
+
+
+def _bytes(case, lo, hi, features):
+    """bench.range_bytes with host counters (the bench counts on the device arrays)."""
+    csr, fmt = case
+    ro = csr.row_offsets.astype(np.int64)
+    return bench.range_bytes(fmt.tasks, lo, hi, fmt.rows, fmt.cols, features, fmt.partial_count,
+                             lambda p0, p1: int(np.count_nonzero(fmt.source_ids[8 * p0:8 * p1] != T.PADDING_SOURCE)),
+                             lambda r0, r1: int(ro[r1] - ro[r0]))
 
 
 @pytest.mark.parametrize("features", [128, 256])
-def test_whole_range_bytes_equal_format_bytes(fmt, features):
-    assert bench.shard_bytes(fmt, 0, fmt.tasks.size, features)["total"] == fmt.algorithmic_bytes(features)["total"]
+def test_whole_range_bytes_equal_format_bytes(case, features):
+    fmt = case[1]
+    got = _bytes(case, 0, fmt.tasks.size, features)
+    want = fmt.algorithmic_bytes(features)
+    for key in ("total", "compulsory", "merge_bytes"):
+        assert got[key] == want[key], key
 
 
 @pytest.mark.parametrize("parts", [2, 3, 8])
-def test_shard_bytes_add_up(fmt, parts):
+def test_shard_bytes_add_up(case, parts):
+    fmt = case[1]
     bounds = T.partition_tasks(fmt, 128, parts)
-    shards = [bench.shard_bytes(fmt, int(bounds[r]), int(bounds[r + 1]), 128) for r in range(parts)]
-    full = bench.shard_bytes(fmt, 0, fmt.tasks.size, 128)
+    shards = [_bytes(case, int(bounds[r]), int(bounds[r + 1]), 128) for r in range(parts)]
+    full = _bytes(case, 0, fmt.tasks.size, 128)
     for key in ("total", "a_bytes", "x_bytes", "y_bytes", "nnz", "rows", "valid_slots", "panels"):
         assert sum(s.get(key, 0) for s in shards) == full[key], key
+
+
+def test_both_arms_print_the_same_config():
+    """The reference arm and this arm describe the workload with the same dict (the driver
+    compares them); neither carries arm-specific keys."""
+    a = bench.workload_config("powerlaw128", 10, 20, 128, 3, 4, 5, 6)
+    b = bench.workload_config("powerlaw128", 10, 20, 128, 3, 4, 5, 6)
+    assert a == b and {"workload", "rows", "nnz", "features"} <= set(a)
+    assert not {"kernel", "task_order", "prep", "format_from", "launch"} & set(a)
+
+
+def test_timed_batches_split_steps():
+    sizes = []
+    for steps in (1, 4, 5, 7, 20, 100):
+        parts = [steps // 5 + (1 if i < steps % 5 else 0) for i in range(5)]
+        sizes.append(sum(p for p in parts if p > 0))
+    assert sizes == [1, 4, 5, 7, 20, 100]
 
 
 @pytest.mark.parametrize("parts", [1, 4, 8, 64])
 def test_window_cuts_start_at_window_boundaries(fmt, parts):
     n = fmt.tasks.size
-    cuts = bench.window_cuts(fmt, 0, n, parts)
+    cuts = bench.window_cuts(fmt.tasks, 0, n, parts)
     assert cuts[0] == 0 and cuts[-1] == n and cuts == sorted(set(cuts))
     sw = fmt.tasks["sw"]
     assert all(sw[c] != sw[c - 1] for c in cuts[1:-1])

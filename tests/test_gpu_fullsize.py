@@ -92,3 +92,9 @@ def test_full_size_device_format_identical(config):
     dev = T.convert_csr_to_sw32_device(csr.rows, csr.cols, up(csr.row_offsets, np.int32),
                                        up(csr.source_ids, np.int32), up(csr.values, np.float32))
     assert dev.differences(fmt) == []
+    if config == "rmat":  # the GPU generator the bench uses gives the same matrix
+        gen = W.generate_device(config)
+        assert gen.nnz == csr.nnz
+        assert torch.equal(gen.row_offsets, up(csr.row_offsets, np.int32))
+        assert torch.equal(gen.source_ids, up(csr.source_ids, np.int32))
+        assert torch.equal(gen.values.view(torch.int32), up(csr.values, np.int32))
