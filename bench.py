@@ -232,8 +232,8 @@ class DeviceWorkload:
         self.prep = {"generate_s": round(t1 - t0, 2), "gpu_convert_ms": round(1e3 * (t2 - t1), 1),
                      "generated_on": "gpu" if W.CONFIGS[name].kind == "rmat" else "host"}
 
-    def config(self, features: int) -> dict:
-        return workload_config(self.name, self.rows, self.nnz, features, self.panels, self.valid_slots,
+    def config(self, features: int, name: str | None = None) -> dict:
+        return workload_config(name or self.name, self.rows, self.nnz, features, self.panels, self.valid_slots,
                                self.tasks.size, self.partial_count)
 
     def bytes(self, lo: int, hi: int, features: int) -> dict:
@@ -694,7 +694,7 @@ def run_config(args, T, W, name, reuse, device, stream, world, rank, threads, ba
     T.check_device()
     ms = max_over_ranks(ms_local) / args.per_config_steps
     local_s = ms_local / args.per_config_steps / 1e3
-    out = {"config": wl.config(F), "ms_per_call": round(ms, 4), "value": wl.nnz * F / (ms / 1e3),
+    out = {"config": wl.config(F, name), "ms_per_call": round(ms, 4), "value": wl.nnz * F / (ms / 1e3),
            "unit": "nnz*F/s", "median_batch_ms": round(max_over_ranks(statistics.median(batch_ms)), 4),
            "hbm_gbs_alg": round(full["total"] / (ms / 1e3) / 1e9, 1),
            "roofline_frac_rank0": round(shard["total"] / local_s / 1e9 / peak, 4),

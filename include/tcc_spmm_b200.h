@@ -198,6 +198,32 @@ int tcc_sw32_host_arrays(const tcc_sw32_host* host, tcc_sw32_arrays* arrays);
 void tcc_sw32_host_free(tcc_sw32_host* host);
 
 /* ---------------------------------------------------------------------------------
+ * Upload of a host format
+ * --------------------------------------------------------------------------------- */
+
+/* A host SW32 format uploaded to one device together with its split-task workspace, owned by
+ * the library. */
+typedef struct tcc_device_matrix tcc_device_matrix;
+
+/* Replaces the constructor of the reference's DeviceMatrix (src/device_matrix.cuh:18-28):
+ * copies every array of a host SW32 format (sizes and host pointers as tcc_sw32_host_sizes and
+ * tcc_sw32_host_arrays give them, or a caller's own arrays laid out the same way) to the current
+ * device and sizes the workspace for `features` (128 or 256): partials = partialCount * 8 *
+ * features floats and counters = windows * (features / 128) u32 set to zero, both only when
+ * partialCount > 0 (NULL otherwise). One device allocation holds everything, each array 256-byte
+ * aligned. The copies run on `stream`, which is synchronised before the call returns, so the host
+ * arrays may be released afterwards. Unlike the launch entry points this call allocates. */
+int tcc_device_matrix_upload(const tcc_sw32_sizes* sizes, const tcc_sw32_arrays* arrays,
+                             uint32_t features, tcc_stream_t stream, tcc_device_matrix** out);
+/* view() and workspace() of the reference's DeviceMatrix (src/device_matrix.cuh:30-37): the
+ * device view of all tasks and the partial/counter pointers (NULL when partialCount is 0). */
+int tcc_device_matrix_view(const tcc_device_matrix* matrix, tcc_sw32_device_view* view);
+int tcc_device_matrix_workspace(const tcc_device_matrix* matrix, float** partials,
+                                uint32_t** counters);
+/* Frees the device memory (the reference's DeviceBuffer destructors). */
+void tcc_device_matrix_free(tcc_device_matrix* matrix);
+
+/* ---------------------------------------------------------------------------------
  * Device format construction
  * --------------------------------------------------------------------------------- */
 

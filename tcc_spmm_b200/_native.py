@@ -118,6 +118,11 @@ SIGNATURES = {
     "tcc_sw32_device_view_of": (C.c_int, [C.c_void_p, C.POINTER(Sw32DeviceView)]),
     "tcc_sw32_device_free": (None, [C.c_void_p]),
     "tcc_sw32_device_trim": (C.c_int, []),
+    "tcc_device_matrix_upload": (C.c_int, [C.POINTER(Sw32Sizes), C.POINTER(Sw32Arrays), C.c_uint32, C.c_void_p,
+                                           C.POINTER(C.c_void_p)]),
+    "tcc_device_matrix_view": (C.c_int, [C.c_void_p, C.POINTER(Sw32DeviceView)]),
+    "tcc_device_matrix_workspace": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "tcc_device_matrix_free": (None, [C.c_void_p]),
 }
 
 # Failure-path test hooks of the library (exported, not declared in the public header).

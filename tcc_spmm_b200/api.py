@@ -393,6 +393,49 @@ class DeviceMatrix:
         return sum(t.numel() * t.element_size() for t in ts if t is not None)
 
 
+class UploadedMatrix:
+    """A host SW32 format uploaded by the library's own upload helper (tcc_device_matrix_upload,
+    the C counterpart of the reference's DeviceMatrix constructor, src/device_matrix.cuh:18-28):
+    one device allocation owned by the library, freed with this object. view() and workspace()
+    as DeviceMatrix's."""
+
+    def __init__(self, fmt: Sw32HostFormat, features: int, stream=None):
+        self._keep = arrays = {
+            "windowOffsets": _u32(fmt.window_offsets), "sourceIds": _u32(fmt.source_ids),
+            "rowGroupMasks": _u32(fmt.row_group_masks),
+            "sourceMetadata": np.ascontiguousarray(fmt.source_metadata, dtype=np.uint64),
+            "values": _f32(fmt.values), "bucketOffsets": _u32(fmt.bucket_offsets),
+            "tasks": np.ascontiguousarray(fmt.tasks), "reductions": np.ascontiguousarray(fmt.reductions),
+            "partialIds": _u32(fmt.partial_ids)}
+        sizes = N.Sw32Sizes(fmt.rows, fmt.cols, fmt.partial_count, int(fmt.bucket_offsets.size > 0),
+                            fmt.window_offsets.size, fmt.source_ids.size, fmt.row_group_masks.size, fmt.values.size,
+                            fmt.bucket_offsets.size, fmt.tasks.size, fmt.reductions.size, fmt.partial_ids.size)
+        ptrs = N.Sw32Arrays(*(arrays[k].ctypes.data if arrays[k].size else None for k in (
+            "windowOffsets", "sourceIds", "rowGroupMasks", "sourceMetadata", "values", "bucketOffsets", "tasks",
+            "reductions", "partialIds")))
+        self.handle = C.c_void_p()
+        self.features = features
+        _check(N.lib().tcc_device_matrix_upload(C.byref(sizes), C.byref(ptrs), features,
+                                                _stream_handle(stream) if stream is not None else None,
+                                                C.byref(self.handle)))
+        self._keep = None
+
+    def view(self) -> N.Sw32DeviceView:
+        v = N.Sw32DeviceView()
+        _check(N.lib().tcc_device_matrix_view(self.handle, C.byref(v)))
+        return v
+
+    def workspace_pointers(self) -> tuple:
+        p, c = C.c_void_p(), C.c_void_p()
+        _check(N.lib().tcc_device_matrix_workspace(self.handle, C.byref(p), C.byref(c)))
+        return p.value or 0, c.value or 0
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            N.lib().tcc_device_matrix_free(self.handle)
+            self.handle = None
+
+
 class _LibraryArray:
     """A device array owned by a library handle, exposed through __cuda_array_interface__
     (torch.as_tensor keeps this object, and so the handle, alive)."""

@@ -25,7 +25,7 @@ CXX = os.environ.get("CXX", "g++")
 CUDA_INCLUDE = Path(NVCC).resolve().parent.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-LIB_SOURCES = ["format.cpp", "capi_host.cpp", "cxx_api.cpp", "features.cu", "spmm.cu", "format_gpu.cu",
+LIB_SOURCES = ["format.cpp", "capi_host.cpp", "cxx_api.cpp", "upload.cpp", "features.cu", "spmm.cu", "format_gpu.cu",
                "matrix_market.cpp"]
 
 

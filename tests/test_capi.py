@@ -92,6 +92,49 @@ def test_static_workspace_checks_before_any_device_work(native):
     assert b"split-window partials need" in native.tcc_last_error()
 
 
+def test_device_matrix_upload_checks_before_any_device_work(native):
+    """tcc_device_matrix_upload (the reference's DeviceMatrix constructor) rejects a bad feature
+    count and inconsistent array sizes before it allocates anything."""
+    csr = T.CsrMatrix(40, 50, *[np.asarray(a) for a in (
+        np.arange(41, dtype=np.uint32), np.arange(40, dtype=np.uint32) % 50, np.ones(40, np.float32))])
+    fmt = T.convert_csr_to_sw32(csr.rows, csr.cols, csr)
+    sizes = N.Sw32Sizes(fmt.rows, fmt.cols, fmt.partial_count, 1, fmt.window_offsets.size, fmt.source_ids.size,
+                        fmt.row_group_masks.size, fmt.values.size, fmt.bucket_offsets.size, fmt.tasks.size,
+                        fmt.reductions.size, fmt.partial_ids.size)
+    arrays = N.Sw32Arrays()
+    out = C.c_void_p()
+    upload = native.tcc_device_matrix_upload
+    assert upload(C.byref(sizes), C.byref(arrays), 64, None, C.byref(out)) == 1
+    assert b"128 or 256" in native.tcc_last_error()
+    assert upload(C.byref(sizes), C.byref(arrays), 128, None, C.byref(out)) == 1
+    assert b"null host array" in native.tcc_last_error()
+    bad = N.Sw32Sizes.from_buffer_copy(sizes)
+    bad.sourceIds += 1
+    assert upload(C.byref(bad), C.byref(arrays), 128, None, C.byref(out)) == 1
+    assert b"8 entries per panel" in native.tcc_last_error()
+    bad = N.Sw32Sizes.from_buffer_copy(sizes)
+    bad.bucketOffsets += 1
+    assert upload(C.byref(bad), C.byref(arrays), 128, None, C.byref(out)) == 1
+    assert b"17 entries per window" in native.tcc_last_error()
+    assert upload(None, C.byref(arrays), 128, None, C.byref(out)) == 1
+    assert out.value is None
+
+
+def test_cpp_device_matrix_header_compiles(tmp_path):
+    """include/tcc_device_matrix.hpp (C++ owner over tcc_device_matrix_*) compiles on its own with
+    the reference's view/workspace types."""
+    src = tmp_path / "t.cpp"
+    src.write_text('#include "tcc_device_matrix.hpp"\n'
+                   "void use(const Sw32HostFormat& m) { tcc::DeviceMatrix d(m, 128); Sw32DeviceView v = d.view();"
+                   " SpmmWorkspace w = d.workspace(); (void)v; (void)w; }\n")
+    import shutil
+
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    cuda_inc = Path(nvcc).resolve().parent.parent / "include"
+    subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+                    "-I", str(cuda_inc), str(src)], check=True)
+
+
 def test_version_string(native):
     assert b"sm_100a" in native.tcc_version()
 
