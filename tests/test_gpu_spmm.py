@@ -156,16 +156,24 @@ def test_bad_feature_count_raises_invalid_argument():
         T.launch_spmm_int8(case.dm.view(), case.packed_dev, case.scales_dev, y, 64, 64, 64, case.dm.workspace())
 
 
+REFERENCE_CASES = sorted(n for n in EDGE_CASES if n != "empty") + ["cpu4096", "powerlaw_small", "stress_small",
+                                                                    "rmat_small"]
+
+
 @pytest.mark.skipif(not O.have_ref_cuda("sm100a"), reason="reference kernel not built")
 @pytest.mark.parametrize("tag", ["sm100a", "sm80"])
 @pytest.mark.parametrize("features", [128, 256])
-def test_matches_reference_kernel(tag, features):
-    """The reference's own kernel on the same inputs (second oracle)."""
+@pytest.mark.parametrize("name", REFERENCE_CASES)
+def test_matches_reference_kernel(name, tag, features):
+    """The reference's own kernel (its src/kernel/spmm.cu, built for sm_100a and as compute_80 PTX)
+    on the same uploaded format, packed X and scales: Y within the stated bound of it, on every
+    edge case and seeded configuration, and the shared counters back at zero after both."""
     torch = _torch()
     if not O.have_ref_cuda(tag):
         pytest.skip(f"reference {tag} build missing")
     ref = O.ref_cuda(tag)
-    case = build_case(W.generate("stress_small"), features, seed=13)
+    csr = W.generate(name) if name in W.CONFIGS else EDGE_CASES[name]()
+    case = build_case(csr, features, seed=13)
     y = run_spmm(case)
     y_ref = torch.full_like(y, float("nan"))
     view = case.dm.view()
@@ -179,7 +187,11 @@ def test_matches_reference_kernel(tag, features):
                          torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     _, bound = oracle_y(case)
-    assert_within_tf32_bound(y.cpu().numpy(), y_ref.cpu().numpy(), bound, f"reference {tag}")
+    got, want = y.cpu().numpy(), y_ref.cpu().numpy()
+    assert np.isfinite(want).all(), "the reference kernel must write every element"
+    assert_within_tf32_bound(got, want, bound, f"{name}/F{features} vs reference {tag}")
+    if case.dm.counters is not None:
+        assert int(case.dm.counters.abs().sum()) == 0, "both kernels return the counters to zero"
 
 
 @pytest.mark.parametrize("features", [128, 256])
