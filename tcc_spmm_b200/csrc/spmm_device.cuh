@@ -275,6 +275,28 @@ __device__ __forceinline__ void mmaTf32Ts(uint32_t dTmem, uint32_t aTmem, unsign
                  ::"r"(dTmem), "r"(aTmem), "l"(bDesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
                  : "memory");
 }
+// The same MMA issued by a whole warp in uniform control flow: one lane, chosen by elect.sync,
+// issues it, so the operands stay warp-uniform. No disable-output-lane mask (every lane of D is
+// written); the instruction descriptor is a compile-time constant.
+template <uint32_t IDESC>
+__device__ __forceinline__ void mmaTf32TsElected(uint32_t dTmem, uint32_t aTmem, unsigned long long bDesc,
+                                                 uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "setp.ne.b32 p, %3, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %4, p;\n\t}"
+                 ::"r"(dTmem), "r"(aTmem), "l"(bDesc), "r"(accumulate), "n"(IDESC)
+                 : "memory");
+}
+// tcgen05.commit issued by one elected lane of a warp in uniform control flow.
+__device__ __forceinline__ void tcCommitElected(uint32_t bar) {
+    asm volatile("{\n\t.reg .pred e;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+                 ::"r"(bar)
+                 : "memory");
+}
+
 // Arrive once on the mbarrier when every tcgen05 operation this thread issued so far is done.
 __device__ __forceinline__ void tcCommit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)

@@ -347,65 +347,79 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         for (uint32_t s = seqA >= L::kARing + pw ? seqA - L::kARing : pw; s < seqA; s += P)
             boundedWait(barL + 8 * (s % L::kARing), (s / L::kARing) & 1);
     } else if (warp == L::kMmaWarp) {
-        // ================================ MMA issuer (one thread) =========================
-        if (lane == 0) {
-            bool ok = true, issued = false;
-            uint32_t seq = 0, windows = 0;
-            // Failure-path test (kTestStallOddCtas): the MMA thread of every odd CTA first waits
-            // on the drain barrier, which nothing completes before the end, so that wait runs out
-            // and the other roles' waits for its commits run out after it. Every wait stays
-            // bounded; the CTA drains its copies, frees its tensor memory and returns.
-            if ((testFlags & kTestStallOddCtas) && (blockIdx.x & 1u))
-                ok = boundedWait(barF, 0);
-            // The next task's panel range is loaded one task ahead, off the MMA issue path.
-            uint32_t nextBegin = 0, nextEnd = 0;
-            if (blockIdx.x < matrix.taskCount) {
-                nextBegin = matrix.tasks[blockIdx.x].begin;
-                nextEnd = matrix.tasks[blockIdx.x].end;
+        // ================================ MMA issuer (one warp) ============================
+        // The whole warp runs the issue loop in uniform control flow and one lane, chosen by
+        // elect.sync, issues each tcgen05 instruction. The issuer is on the critical chain of every
+        // chunk (A columns and B tiles in, commit out) and shares its SM sub-partition with seven
+        // other warps, so its instruction count per chunk is kept minimal: descriptors stepped by
+        // a constant, the instruction descriptor an immediate, full chunks fully unrolled.
+        bool ok = true, issued = false;
+        uint32_t seq = 0, windows = 0;
+        // Failure-path test (kTestStallOddCtas): the MMA warp of every odd CTA first waits on the
+        // drain barrier, which nothing completes before the end, so that wait runs out and the
+        // other roles' waits for its commits run out after it. Every wait stays bounded; the CTA
+        // drains its copies, frees its tensor memory and returns.
+        if ((testFlags & kTestStallOddCtas) && (blockIdx.x & 1u))
+            ok = boundedWait(barF, 0);
+        const unsigned long long desc0 = bTileDesc(base + L::kBOff);
+        constexpr uint32_t kTileStep = L::kBTileBytes >> 4; // descriptor units between B tiles
+        // The next task's panel range is loaded one task ahead, off the MMA issue path.
+        uint32_t nextBegin = 0, nextEnd = 0;
+        if (blockIdx.x < matrix.taskCount) {
+            nextBegin = matrix.tasks[blockIdx.x].begin;
+            nextEnd = matrix.tasks[blockIdx.x].end;
+        }
+        for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
+            const uint32_t panelCount = nextEnd - nextBegin;
+            if (tk + gridDim.x < matrix.taskCount) {
+                nextBegin = matrix.tasks[tk + gridDim.x].begin;
+                nextEnd = matrix.tasks[tk + gridDim.x].end;
             }
-            for (uint64_t tk = blockIdx.x; tk < matrix.taskCount; tk += gridDim.x) {
-                const uint32_t panelCount = nextEnd - nextBegin;
-                if (tk + gridDim.x < matrix.taskCount) {
-                    nextBegin = matrix.tasks[tk + gridDim.x].begin;
-                    nextEnd = matrix.tasks[tk + gridDim.x].end;
-                }
-                if (panelCount == 0)
-                    continue;
-                if (ok && windows >= 1 && !boundedWait(barR, (windows - 1) & 1))
+            if (panelCount == 0)
+                continue;
+            if (ok && windows >= 1 && !boundedWait(barR, (windows - 1) & 1))
+                ok = false;
+            ++windows;
+            dev::tcFenceAfter();
+            const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
+            for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
+                // These waits are on the critical path: suspend on the barrier (resumes at once)
+                // rather than sleep between polls.
+                if (ok && (!boundedWait(barA, seq & 1) || !boundedWait(barB, seq & 1)))
                     ok = false;
-                ++windows;
+                if (!ok)
+                    continue;
                 dev::tcFenceAfter();
-                const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
-                for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
-                    // With one stage these waits are on the critical path: suspend on the barrier
-                    // (resumes at once) rather than sleep between polls.
-                    if (ok && (!boundedWait(barA, seq & 1) || !boundedWait(barB, seq & 1)))
-                        ok = false;
-                    if (!ok)
-                        continue;
-                    dev::tcFenceAfter();
-                    const uint32_t inChunk = min(uint32_t(kChunk8), panelCount - ch * kChunk8);
-                    for (uint32_t pp = 0; pp < inChunk; ++pp) {
-                        const unsigned long long desc = bTileDesc(base + L::kBOff + pp * L::kBTileBytes);
+                const uint32_t inChunk = min(uint32_t(kChunk8), panelCount - ch * kChunk8);
+                if (inChunk == kChunk8) {
+#pragma unroll
+                    for (uint32_t pp = 0; pp < kChunk8; ++pp)
 #pragma unroll
                         for (int sl = 0; sl < L::kSlices; ++sl)
-                            dev::mmaTf32Ts(tmem + sl * L::kSliceCols + 8 * kChunk8, tmem + sl * L::kSliceCols + 8 * pp,
-                                           desc, L::kIdesc, (ch | pp) != 0);
-                    }
-                    issued = true;
-                    dev::tcCommit(barS + 8 * (seq & 1));
+                            dev::mmaTf32TsElected<L::kIdesc>(tmem + sl * L::kSliceCols + 8 * kChunk8,
+                                                             tmem + sl * L::kSliceCols + 8 * pp,
+                                                             desc0 + pp * kTileStep, (ch | pp) != 0);
+                } else {
+                    for (uint32_t pp = 0; pp < inChunk; ++pp)
+#pragma unroll
+                        for (int sl = 0; sl < L::kSlices; ++sl)
+                            dev::mmaTf32TsElected<L::kIdesc>(tmem + sl * L::kSliceCols + 8 * kChunk8,
+                                                             tmem + sl * L::kSliceCols + 8 * pp,
+                                                             desc0 + pp * kTileStep, (ch | pp) != 0);
                 }
-                if (ok)
-                    dev::tcCommit(barD);
+                issued = true;
+                dev::tcCommitElected(barS + 8 * (seq & 1));
             }
-            if (issued) { // every MMA is complete before the tensor memory is released
-                dev::tcCommit(barF);
-                if (!boundedWait(barF, 0))
-                    ok = false;
-            }
-            if (!ok)
-                flags[1] = 1;
+            if (ok)
+                dev::tcCommitElected(barD);
         }
+        if (issued) { // every MMA is complete before the tensor memory is released
+            dev::tcCommitElected(barF);
+            if (!boundedWait(barF, 0))
+                ok = false;
+        }
+        if (!ok)
+            flags[1] = 1;
         __syncwarp();
     } else {
         // ==================================== consumers ===================================
