@@ -41,6 +41,9 @@ CONFIGS = {
                      "values U(0,1], F128"),
     "rmat": Config("rmat", "rmat", 128, (24, 1 << 29, 0.57, 0.19, 0.19), 24,
                    "R-MAT(0.57,0.19,0.19,0.05), 2^24 rows, 2^29 edge samples, duplicates merged, values 1/deg_i, F128"),
+    # A reduced power-law matrix for profiler captures: X (134 MB at F128) still exceeds L2.
+    "powerlaw_profile": Config("powerlaw_profile", "powerlaw", 128, (1048576, 1048576 * 51, 2.1, 17000, 0.6, 4096),
+                               1048576, "1,048,576-row power-law matrix, mean degree 51 (profiler captures)"),
     # Scaled-down shapes of the same generators (tests).
     "powerlaw_small": Config("powerlaw_small", "powerlaw", 128, (65536, 65536 * 51, 2.1, 4000, 0.6, 4096), 7,
                              "65,536-row power-law matrix, mean degree 51"),
