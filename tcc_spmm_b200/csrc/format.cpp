@@ -382,12 +382,18 @@ CsrMatrix canonicalCsr(std::uint32_t rows, std::uint32_t cols, std::uint32_t nnz
     return out;
 }
 
-// Estimated cost of a task: its panels weighted by the row-group MMAs they issue, plus a fixed
-// write-back term per task.
+// Estimated cost of a task, in units of about one panel's share of a chunk: the fast kernel works
+// in 8-panel chunks, and a partly filled chunk costs about as much as a full one (80 per chunk);
+// a panel whose sources touch several 8-row groups scatters more B entries (2 per extra group);
+// and every task pays its window epilogue (accumulator read-out and row stores, about 2.7 chunks'
+// time at F = 128 in a per-phase profile of the kernel: 220; a chunk of F = 256 carries two
+// feature slices while the epilogue's length stays, so the term halves relative to the chunks).
 double taskCost(const tcc_sw32_task& task, const std::uint32_t* masks, std::uint32_t features) {
-    double cost = 16.0 * (features / 128.0);
-    for (std::uint32_t p = task.begin; p < task.end; ++p)
-        cost += 8.0 + (masks ? 2.0 * __builtin_popcount(masks[p] & 15u) : 3.0);
+    const std::uint32_t panels = task.end - task.begin;
+    double cost = 220.0 * 128.0 / std::max(128u, features) + 80.0 * ((panels + 7) / 8);
+    if (masks)
+        for (std::uint32_t p = task.begin; p < task.end; ++p)
+            cost += 2.0 * (__builtin_popcount(masks[p] & 15u) - 1);
     return cost;
 }
 
