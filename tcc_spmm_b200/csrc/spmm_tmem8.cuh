@@ -30,24 +30,29 @@
 //
 // Roles (chunks of the CTA's tasks b, b+G, ... form one stream; producer pw owns chunks pw,
 // pw+P, ...):
-//   consumers 0..F/32-1  warp w owns TMEM lane quarter w%4 of slice w/4 (32 features). X step
-//                        (kPrefetch chunks ahead): cp.async of its 32 bytes of the chunk's 64
-//                        source rows into a 32-byte-stride ring; within each panel row r is
-//                        stored at position r/2 + 4(r%2), so the two rows a lane reads (2c and
-//                        2c + 1) of all lanes fall in different banks. Then the A columns.
-//   producers (P warps)  A step (bulk copies of the chunk's 64 IDs and metadata words), V step
-//                        (cp.async of the value range and 64 scales; each lane two slots), B
-//                        step (the chunk's 8 B tiles in the one shared-memory B buffer).
-//   MMA warp             one thread issues the chunk's MMAs and the commits.
+//   producers (P warps)  A step (bulk copies of the chunk's 64 IDs and metadata words, kALead
+//                        chunks ahead), V step (kVLead ahead: cp.async of the value range and the
+//                        64 scales, and of the chunk's 64 whole source rows into the shared X ring,
+//                        16 bytes per lane, F / 16 lanes per row), B step (the chunk's 8 B tiles in
+//                        the one shared-memory B buffer).
+//   consumers 0..F/32-1  warp w owns TMEM lane quarter w%4 of slice w/4 (32 features): it reads its
+//                        32 bytes of the chunk's rows from the X ring and stores the A columns. It
+//                        touches no global memory in the chunk loop.
+//   MMA warp             runs the issue loop as a warp; one elected lane issues the chunk's MMAs and
+//                        the commits.
+// The X ring keeps rows at a stride of F + 16 bytes, so the rows 2c and 2c + 1 that lane group c
+// reads fall in distinct banks. Gathering whole rows in the producers instead of 32-byte quarters
+// in each consumer took about 1,000 cycles per chunk off the consumers, the critical role, and
+// made a warp-wide copy touch 4 lines instead of 16.
 // Synchronisation: bFull (producer -> MMA: B tiles written), aFull (consumers -> MMA: A columns
 // stored), sFree[c % 2] (MMA commit of chunk c -> the producer and the consumers of chunk c + 1,
 // who then refill the B tiles and the A columns at the same time), dFull/dFree for the
-// accumulator, aLand/aUsed and vFull for the producer rings. All waits bounded.
+// accumulator, aLand and vFull for the producer rings, xFull (the owning producer's copies of a
+// chunk's rows have landed) and xFree (consumers -> producers: the X slot may be refilled). A
+// slots are read only by the producer that fills them. All waits bounded.
 // Every copy uses the default L2 policy: evict-last on X and evict-first on the format arrays
-// cost 3%. The X copies keep the 128-byte L2 prefetch. Invalid slots issue no copy at all: the
-// consumer stores zeros to shared memory, and the producer skips their scales. A zero-size copy
-// from one shared dummy address per invalid slot made every SM queue on that one address (5%
-// slower on power-law F128; for the scales 2%), and a full copy of a dummy row 60%.
+// cost 3%. Invalid slots issue no copy at all: their A columns keep stale (finite) bytes, which
+// meet all-zero rows of B, and the producer skips their scales.
 #pragma once
 #include "spmm_persistent.cuh"
 
@@ -84,13 +89,18 @@ template <int F, int P> struct Tmem8 {
     static constexpr int kMmaWarp = kConsumers + P;
     static constexpr int kThreads = 32 * (kConsumers + P + 1);
     static constexpr int kSlots = 8 * kChunk8;
-    // Consumer X rings (one per consumer warp): 64 rows x 32 bytes per chunk.
+    // X ring, shared by the consumers: kXDepth chunks of 64 whole packed source rows. Row r of a
+    // chunk sits at r * (F + 16): the 16-byte pad puts rows 2c and 2c + 1, which lane group c
+    // reads, in distinct banks. The producer that owns a chunk copies its rows (kLanesPerRow
+    // lanes of 16 bytes per row, kRowsPerCopy rows per warp-wide cp.async).
     static constexpr int kXDepth = 3;
-    static constexpr int kPrefetch = kXDepth - 1;
-    static constexpr int kXSlotBytes = kSlots * 32;
+    static constexpr int kXRowStride = F + 16;
+    static constexpr int kXSlotBytes = kSlots * kXRowStride;
+    static constexpr int kLanesPerRow = F / 16;
+    static constexpr int kRowsPerCopy = 32 / kLanesPerRow;
     // Producer rings.
     static constexpr int kALead = 5, kARing = 8;
-    static constexpr int kVLead = 3, kVRing = 4;
+    static constexpr int kVLead = 2, kVRing = 4;
     static constexpr int kVCap = 256;
     static constexpr int kHeaderOff = 4 * kSlots + 8 * kSlots;  // after ids and metadata
     static constexpr int kASlotBytes = kHeaderOff + 16;
@@ -98,14 +108,14 @@ template <int F, int P> struct Tmem8 {
     static constexpr int kBTileBytes = 2048;
     static constexpr int kBOff = 0;
     static constexpr int kXOff = kBOff + kChunk8 * kBTileBytes;
-    static constexpr int kAOff = kXOff + kConsumers * kXDepth * kXSlotBytes;
+    static constexpr int kAOff = kXOff + kXDepth * kXSlotBytes;
     static constexpr int kVOff = kAOff + kARing * kASlotBytes;
     static constexpr int kVBaseOff = kVOff + kVRing * kVSlotBytes;
     static constexpr int kFlagOff = kVBaseOff + 32;
     static constexpr int kBarOff = kFlagOff + 16;
-    // bFull, aFull, sFree [2] (by chunk parity); dFull, dFree (two words reserved each); aLand,
-    // aUsed [kARing]; vFull [kVRing]; drain
-    static constexpr int kBars = 4 + 4 + 2 * kARing + kVRing + 1;
+    // bFull, aFull, sFree [2] (by chunk parity); dFull, dFree (two words reserved each); aLand
+    // [kARing]; vFull [kVRing]; xFull, xFree [kXDepth]; drain
+    static constexpr int kBars = 4 + 4 + kARing + kVRing + 2 * kXDepth + 1;
     static constexpr int kBytes = kBarOff + 8 * kBars;
     // Tensor memory per slice: the A stage (64 columns: 8 panels x 8 sources) and the
     // accumulator (64 columns).
@@ -114,55 +124,16 @@ template <int F, int P> struct Tmem8 {
     static constexpr int kTmemCols = kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
     static constexpr int kMaxCtasPerSm = 512 / kTmemCols;
     static_assert(kColsUsed <= 512, "tensor memory");
-    static_assert(kVRing <= 8 && kARing >= kALead + 2 && kVRing > kVLead && kALead > kVLead && kPrefetch <= kALead,
+    static_assert(kVRing <= 8 && kARing >= kALead + 2 && kVRing > kVLead && kALead > kVLead && kXDepth > kVLead,
                   "rings");
+    static_assert(kXRowStride % 16 == 0 && (kXRowStride / 2) % 32 == 8 && kSlots % kRowsPerCopy == 0,
+                  "X rows: 16-byte aligned, conflict-free reads");
     static_assert(kARing % P == 0 && kVRing % P == 0, "every ring slot has one producer");
     static_assert(P == 1 || P == 2, "sFree[c % 2] gives each producer consecutive phases only for P <= 2");
     static_assert(kASlotBytes % 16 == 0 && kXOff % 16 == 0 && kAOff % 16 == 0 && kVOff % 16 == 0 && kBarOff % 8 == 0,
                   "alignment");
     static constexpr uint32_t kIdesc = kIdescTf32M128N64;
 };
-
-// Position of row r (0..63) of a chunk in the consumer's X slot: within each panel (8 rows) the
-// even rows come first, so rows 2c and 2c + 1 of the four lane groups c hit distinct banks.
-__device__ __forceinline__ uint32_t xRowSlot(uint32_t row) {
-    return (row & ~7u) + ((row & 7u) >> 1) + 4 * (row & 1u);
-}
-
-// Consumer X step of chunk s: warp w gathers bytes 32w..32w+31 of the chunk's 64 packed source
-// rows (two 16-byte cp.async per row; zeros stored for invalid slots) as one cp.async group, then
-// tells the producer that the chunk's IDs have been read. Returns false when the wait ran out.
-template <int F, int P>
-__device__ __forceinline__ bool gatherSlice8(unsigned char* smem, uint32_t xring, uint32_t barLand, uint32_t barUsed,
-                                             const int8_t* __restrict__ packedX, uint32_t cols, uint32_t total,
-                                             uint32_t s, int lane, int w, bool ok) {
-    using L = Tmem8<F, P>;
-    if (ok && s < total) {
-        const uint32_t aslot = s % L::kARing;
-        if (!boundedWait(barLand + 8 * aslot, (s / L::kARing) & 1)) {
-            ok = false;
-        } else {
-            const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
-            const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
-            const uint32_t dst = xring + (s % L::kXDepth) * L::kXSlotBytes;
-#pragma unroll
-            for (int pass = 0; pass < 4; ++pass) {
-                const uint32_t row = pass * 16 + (lane >> 1), piece = lane & 1;
-                const uint32_t id = (row >> 3) < np ? reinterpret_cast<const uint32_t*>(a)[row] : 0xFFFFFFFFu;
-                const uint32_t d = dst + xRowSlot(row) * 32 + 16 * piece;
-                if (id < cols)
-                    dev::cpAsync16Line(d, packedX + uint64_t(id) * F + 32 * w + 16 * piece, 16u);
-                else
-                    dev::stsZero16(d);
-            }
-            __syncwarp();
-            if (lane == 0)
-                dev::mbarArrive(barUsed + 8 * aslot);
-        }
-    }
-    dev::cpAsyncCommit();
-    return ok;
-}
 
 template <int F, int P>
 __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPerSm)
@@ -180,9 +151,10 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
     const uint32_t barD = barS + 16;           // dFull [2]
     const uint32_t barR = barD + 16;           // dFree [2]
     const uint32_t barL = barR + 16;           // aLand [kARing]
-    const uint32_t barU = barL + 8 * L::kARing; // aUsed [kARing]
-    const uint32_t barV = barU + 8 * L::kARing; // vFull [kVRing]
-    const uint32_t barF = barV + 8 * L::kVRing; // drain
+    const uint32_t barV = barL + 8 * L::kARing;    // vFull [kVRing]
+    const uint32_t barXF = barV + 8 * L::kVRing;   // xFull [kXDepth]
+    const uint32_t barXE = barXF + 8 * L::kXDepth; // xFree [kXDepth]
+    const uint32_t barF = barXE + 8 * L::kXDepth;  // drain
     volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(smem + L::kFlagOff);
     if (threadIdx.x == 0) {
         dev::mbarInit(barB, 1);
@@ -195,10 +167,13 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         }
         for (int s = 0; s < L::kARing; ++s) {
             dev::mbarInit(barL + 8 * s, 1);
-            dev::mbarInit(barU + 8 * s, L::kConsumers);
         }
         for (int s = 0; s < L::kVRing; ++s)
             dev::mbarInit(barV + 8 * s, 32);
+        for (int s = 0; s < L::kXDepth; ++s) {
+            dev::mbarInit(barXF + 8 * s, 32); // the owning producer's lanes, once their copies land
+            dev::mbarInit(barXE + 8 * s, L::kConsumers);
+        }
         dev::mbarInit(barF, 1);
         flags[0] = flags[1] = flags[3] = 0; // flags[2] receives the TMEM address (allocating warp)
         dev::fenceBarrierInit();
@@ -226,11 +201,9 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         for (uint32_t seqF = pw; seqF < total && ok; seqF += P) {
             // ---- A steps: IDs and metadata of chunks up to seqF + kALead (one lane) ----
             for (; seqA < total && seqA <= seqF + L::kALead; seqA += P) {
+                // The slot's previous chunk, seqA - kARing, belongs to this producer too (kARing is a
+                // multiple of P), and its V and B steps are done: no other role reads A slots.
                 const uint32_t slot = seqA % L::kARing;
-                if (seqA >= uint32_t(L::kARing) && !boundedWait(barU + 8 * slot, ((seqA / L::kARing) - 1) & 1)) {
-                    ok = false;
-                    break;
-                }
                 const uint32_t p0 = walk.next;
                 const uint32_t np = min(uint32_t(kChunk8), walk.end - p0);
                 if (lane == 0) {
@@ -252,10 +225,14 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             if (!ok)
                 break;
             __syncwarp();
-            // ---- V steps: value ranges and scales of chunks up to seqF + kVLead ----
+            // ---- V steps: value ranges, scales and X rows of chunks up to seqF + kVLead; the X
+            // rows of chunk s go to X slot s % kXDepth once the consumers have released chunk
+            // s - kXDepth from it ----
             for (; seqV < seqA && seqV <= seqF + L::kVLead; seqV += P) {
-                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing;
-                if (!boundedWait(barL + 8 * aslot, (seqV / L::kARing) & 1)) {
+                const uint32_t aslot = seqV % L::kARing, vslot = seqV % L::kVRing, xslot = seqV % L::kXDepth;
+                if (!boundedWait(barL + 8 * aslot, (seqV / L::kARing) & 1) ||
+                    (seqV >= uint32_t(L::kXDepth) &&
+                     !boundedWait(barXE + 8 * xslot, ((seqV / L::kXDepth) - 1) & 1))) {
                     ok = false;
                     break;
                 }
@@ -263,11 +240,13 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
                 const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
                 uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+                uint32_t ids[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const uint32_t slot = lane + 32 * h;
                     const bool inRange = (slot >> 3) < np;
                     const uint32_t id = inRange ? reinterpret_cast<const uint32_t*>(a)[slot] : 0xFFFFFFFFu;
+                    ids[h] = id;
                     const uint64_t meta =
                         inRange ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
                     if (id < cols) // an invalid slot's scale is never read (its row mask is empty)
@@ -288,6 +267,18 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                     for (uint32_t i = lane; i < count; i += 32)
                         dev::cpAsync4(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4);
                 dev::cpAsyncArriveNoinc(barV + 8 * vslot);
+                // X rows: whole rows, kLanesPerRow lanes of 16 bytes each; an invalid slot copies
+                // nothing (its A columns keep stale, finite bytes, which meet an all-zero row of B).
+                const uint32_t xdst = base + L::kXOff + xslot * L::kXSlotBytes + 16 * (lane % L::kLanesPerRow);
+                const int8_t* xsrc = packedX + 16 * (lane % L::kLanesPerRow);
+#pragma unroll
+                for (int i = 0; i < L::kSlots / L::kRowsPerCopy; ++i) {
+                    const uint32_t row = L::kRowsPerCopy * i + lane / L::kLanesPerRow;
+                    const uint32_t id = __shfl_sync(0xFFFFFFFFu, ids[(L::kRowsPerCopy * i) >> 5], row & 31);
+                    if (id < cols)
+                        dev::cpAsync16Line(xdst + row * L::kXRowStride, xsrc + uint64_t(id) * F, 16u);
+                }
+                dev::cpAsyncArriveNoinc(barXF + 8 * xslot);
             }
             if (!ok)
                 break;
@@ -425,16 +416,14 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         // ==================================== consumers ===================================
         const int quarter = warp & 3, slice = warp >> 2;
         const int g = lane >> 2, c = lane & 3;
-        const uint32_t xring = base + L::kXOff + warp * L::kXDepth * L::kXSlotBytes;
         const uint32_t tLane = uint32_t(32 * quarter) << 16;
         const uint32_t aTmem = tmem + slice * L::kSliceCols + tLane;
         const uint32_t dTmem = tmem + slice * L::kSliceCols + 8 * kChunk8 + tLane;
         const uint32_t feature = slice * 128 + 32 * quarter + tmemLaneFeature(lane);
-        // Rows 2c and 2c + 1 of panel pp sit at positions 8pp + c and 8pp + 4 + c.
-        const uint32_t xLane = xring + 4 * g + 32 * c;
+        // Word g of this warp's 32 bytes (128 * slice + 32 * quarter) of row 2c of panel 0; row
+        // 2c + 1 follows one row stride later, panel pp 8 row strides later.
+        const uint32_t xLane = base + L::kXOff + 2 * c * L::kXRowStride + 32 * warp + 4 * g;
         bool ok = true;
-        for (uint32_t s = 0; s < uint32_t(L::kPrefetch); ++s)
-            ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, s, lane, warp, ok);
         uint32_t seq = 0, windows = 0;
         tcc_sw32_task nextTask{};
         if (blockIdx.x < matrix.taskCount)
@@ -446,26 +435,24 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             const uint32_t panelCount = task.end - task.begin;
             const uint32_t nch = (panelCount + kChunk8 - 1) / kChunk8;
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
-                ok = gatherSlice8<F, P>(smem, xring, barL, barU, packedX, cols, total, seq + L::kPrefetch, lane, warp,
-                                        ok);
-                dev::cpAsyncWaitGroup<L::kPrefetch>();
-                __syncwarp();
-                // The MMAs of chunk seq - 1 are complete: the A columns may be rewritten (the
-                // producer refills the B tiles at the same time).
-                if (ok && seq >= 1 && !boundedWait(barS + 8 * ((seq - 1) & 1), ((seq - 1) >> 1) & 1))
+                // The chunk's X rows have landed, and the MMAs of chunk seq - 1 are complete: the A
+                // columns may be rewritten (the producer refills the B tiles at the same time).
+                const uint32_t xslot = seq % L::kXDepth;
+                if (ok && (!boundedWait(barXF + 8 * xslot, (seq / L::kXDepth) & 1) ||
+                           (seq >= 1 && !boundedWait(barS + 8 * ((seq - 1) & 1), ((seq - 1) >> 1) & 1))))
                     ok = false;
                 if (!ok)
                     continue;
                 dev::tcFenceAfter();
-                const uint32_t xs = xLane + (seq % L::kXDepth) * L::kXSlotBytes;
+                const uint32_t xs = xLane + xslot * L::kXSlotBytes;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t lo[16], hi[16];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int pp = 4 * half + q;
-                        const uint32_t wa = dev::ldsU32(xs + 256 * pp) ^ 0x80808080u;
-                        const uint32_t wb = dev::ldsU32(xs + 256 * pp + 128) ^ 0x80808080u;
+                        const uint32_t wa = dev::ldsU32(xs + 8 * L::kXRowStride * pp) ^ 0x80808080u;
+                        const uint32_t wb = dev::ldsU32(xs + 8 * L::kXRowStride * pp + L::kXRowStride) ^ 0x80808080u;
                         dev::int8PairToFloat<0>(wa, wb, lo[4 * q + 0], lo[4 * q + 1]);
                         dev::int8PairToFloat<1>(wa, wb, lo[4 * q + 2], lo[4 * q + 3]);
                         dev::int8PairToFloat<2>(wa, wb, hi[4 * q + 0], hi[4 * q + 1]);
@@ -477,8 +464,10 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 dev::tcWaitSt();
                 dev::tcFenceBefore();
                 __syncwarp();
-                if (lane == 0)
+                if (lane == 0) {
                     dev::mbarArrive(barA);
+                    dev::mbarArrive(barXE + 8 * xslot); // the chunk's X rows are read
+                }
             }
             // ---- epilogue of this window ----
             const uint32_t rowBase = task.sw * 32;
@@ -567,7 +556,6 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             }
             namedBarrier(1, 32 * L::kConsumers); // flags[0] is reused by the next split task
         }
-        dev::cpAsyncWaitAll();
         if (!ok)
             flags[1] = 1;
     }

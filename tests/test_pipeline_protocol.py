@@ -1,7 +1,7 @@
 """Model check of the mbarrier hand-offs of the 8-panel tensor-memory kernel (CPU only).
 
-`spmm_tmem8.cuh` (2 producer warps, 4 consumer warps) orders its roles with mbarriers waited on
-by phase parity
+`spmm_tmem8.cuh` (2 producer warps that also gather the X rows, 4 consumer warps) orders its
+roles with mbarriers waited on by phase parity
 (`mbarrier.try_wait.parity`). A parity wait cannot tell a phase from the one two ahead, so the
 phase a role waits for must be the barrier's current phase or the one just completed. This test
 restates, per role, the sequence of waits and arrivals the kernels perform for one CTA's stream
@@ -34,11 +34,12 @@ class Shape:
     a_lead: int
     v_ring: int
     v_lead: int
-    prefetch: int     # consumer X prefetch in chunks
+    x_ring: int       # X ring slots (the V step of chunk s waits until chunk s - x_ring is released)
 
 
-TMEM8 = Shape(producers=2, consumers=4, sfree=2, a_ring=8, a_lead=5, v_ring=4, v_lead=3, prefetch=2)
-SINGLE_SFREE = Shape(producers=2, consumers=4, sfree=1, a_ring=8, a_lead=5, v_ring=4, v_lead=3, prefetch=2)
+TMEM8 = Shape(producers=2, consumers=4, sfree=2, a_ring=8, a_lead=5, v_ring=4, v_lead=2, x_ring=3)
+SINGLE_SFREE = Shape(producers=2, consumers=4, sfree=1, a_ring=8, a_lead=5, v_ring=4, v_lead=2, x_ring=3)
+SHALLOW_X = Shape(producers=2, consumers=4, sfree=2, a_ring=8, a_lead=5, v_ring=4, v_lead=2, x_ring=1)
 
 
 class Aliased(AssertionError):
@@ -68,14 +69,14 @@ def producer(pw, s: Shape, total, bars):
     seq_a = seq_v = pw
     for seq_f in range(pw, total, s.producers):
         while seq_a < total and seq_a <= seq_f + s.a_lead:             # A steps (IDs, metadata)
-            slot = seq_a % s.a_ring
-            if seq_a >= s.a_ring:
-                yield bars["aUsed"][slot], seq_a // s.a_ring - 1
-            bars["aLand"][slot].arrive()
+            bars["aLand"][seq_a % s.a_ring].arrive()
             seq_a += s.producers
-        while seq_v < seq_a and seq_v <= seq_f + s.v_lead:             # V steps (values, scales)
+        while seq_v < seq_a and seq_v <= seq_f + s.v_lead:             # V steps (values, scales, X)
             yield bars["aLand"][seq_v % s.a_ring], seq_v // s.a_ring
+            if seq_v >= s.x_ring:
+                yield bars["xFree"][seq_v % s.x_ring], seq_v // s.x_ring - 1
             bars["vFull"][seq_v % s.v_ring].arrive()
+            bars["xFull"][seq_v % s.x_ring].arrive()
             seq_v += s.producers
         yield bars["vFull"][seq_f % s.v_ring], seq_f // s.v_ring        # B step
         if seq_f >= 1:
@@ -84,20 +85,14 @@ def producer(pw, s: Shape, total, bars):
 
 
 def consumer(s: Shape, tasks, total, bars):
-    def gather(c):
-        if c < total:
-            yield bars["aLand"][c % s.a_ring], c // s.a_ring
-            bars["aUsed"][c % s.a_ring].arrive()
-
-    for c in range(s.prefetch):
-        yield from gather(c)
     seq = windows = 0
     for chunks in tasks:
         for _ in range(chunks):
-            yield from gather(seq + s.prefetch)
+            yield bars["xFull"][seq % s.x_ring], seq // s.x_ring
             if seq >= 1:
                 yield bars["sFree"][(seq - 1) % s.sfree], (seq - 1) // s.sfree
             bars["aFull"].arrive()
+            bars["xFree"][seq % s.x_ring].arrive()
             seq += 1
         if chunks:
             yield bars["dFull"], windows
@@ -128,8 +123,9 @@ def run(s: Shape, tasks, rng: random.Random) -> None:
         "sFree": [Barrier(f"sFree{i}", 1) for i in range(s.sfree)],
         "dFull": Barrier("dFull", 1), "dFree": Barrier("dFree", s.consumers),
         "aLand": [Barrier(f"aLand{i}", 1) for i in range(s.a_ring)],
-        "aUsed": [Barrier(f"aUsed{i}", s.consumers) for i in range(s.a_ring)],
         "vFull": [Barrier(f"vFull{i}", 1) for i in range(s.v_ring)],
+        "xFull": [Barrier(f"xFull{i}", 1) for i in range(s.x_ring)],
+        "xFree": [Barrier(f"xFree{i}", s.consumers) for i in range(s.x_ring)],
     }
     roles = [producer(p, s, total, bars) for p in range(s.producers)]
     roles += [consumer(s, tasks, total, bars) for _ in range(s.consumers)]
@@ -177,3 +173,17 @@ def test_single_sfree_barrier_aliases():
             except Aliased:
                 hit = True
     assert hit, "a single sFree barrier with two producers must be caught"
+
+
+def test_x_ring_must_outlast_the_v_lead():
+    """With one X slot, the V step of chunk s (issued kVLead chunks ahead of the B step) waits for
+    the consumers to release chunk s - 1, which needs the B tiles of chunk s - 1: the roles
+    deadlock or alias. The kernel's static_assert requires kXDepth > kVLead."""
+    caught = False
+    for k, tasks in enumerate(task_lists(5)):
+        for trial in range(10):
+            try:
+                run(SHALLOW_X, tasks, random.Random(100 * k + trial))
+            except (Aliased, AssertionError):
+                caught = True
+    assert caught
