@@ -100,6 +100,12 @@ __device__ __forceinline__ void mbarInit(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbarArrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// Arrive on `bar` in the threads where `pred` holds, as one predicated instruction (no branch).
+__device__ __forceinline__ void mbarArriveIf(bool pred, uint32_t bar) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %1, 0;\n\t@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(bar),
+                 "r"(static_cast<uint32_t>(pred))
+                 : "memory");
+}
 __device__ __forceinline__ bool mbarTryWait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile("{\n\t.reg .pred p;\n\t"

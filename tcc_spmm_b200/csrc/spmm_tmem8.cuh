@@ -425,6 +425,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         const uint32_t xLane = base + L::kXOff + 2 * c * L::kXRowStride + 32 * warp + 4 * g;
         bool ok = true;
         uint32_t seq = 0, windows = 0;
+        uint32_t xSlot = 0, xPhase = 0; // X slot of chunk seq (seq % kXDepth) and its phase parity
         tcc_sw32_task nextTask{};
         if (blockIdx.x < matrix.taskCount)
             nextTask = matrix.tasks[blockIdx.x];
@@ -437,8 +438,12 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             for (uint32_t ch = 0; ch < nch; ++ch, ++seq) {
                 // The chunk's X rows have landed, and the MMAs of chunk seq - 1 are complete: the A
                 // columns may be rewritten (the producer refills the B tiles at the same time).
-                const uint32_t xslot = seq % L::kXDepth;
-                if (ok && (!boundedWait(barXF + 8 * xslot, (seq / L::kXDepth) & 1) ||
+                const uint32_t xslot = xSlot, xparity = xPhase;
+                if (++xSlot == uint32_t(L::kXDepth)) {
+                    xSlot = 0;
+                    xPhase ^= 1u;
+                }
+                if (ok && (!boundedWait(barXF + 8 * xslot, xparity) ||
                            (seq >= 1 && !boundedWait(barS + 8 * ((seq - 1) & 1), ((seq - 1) >> 1) & 1))))
                     ok = false;
                 if (!ok)
@@ -464,10 +469,8 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 dev::tcWaitSt();
                 dev::tcFenceBefore();
                 __syncwarp();
-                if (lane == 0) {
-                    dev::mbarArrive(barA);
-                    dev::mbarArrive(barXE + 8 * xslot); // the chunk's X rows are read
-                }
+                dev::mbarArriveIf(lane == 0, barA);
+                dev::mbarArriveIf(lane == 0, barXE + 8 * xslot); // the chunk's X rows are read
             }
             // ---- epilogue of this window ----
             const uint32_t rowBase = task.sw * 32;
@@ -498,6 +501,16 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 }
                 if (!haveWs)
                     continue;
+                if (!split && rowBase + 32 <= rows) {
+                    // Unsplit window with all 32 rows in range (all but the last window): 16
+                    // branch-free stores at constant offsets from one row pointer. The epilogue
+                    // sits between a window's last commit and the next window's first A columns.
+                    float* out = output + uint64_t(rowBase + 16 * half) * F + feature;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        __stcs(out + j * F, __uint_as_float(h[j]) + __uint_as_float(l[j]));
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int row = 16 * half + j;
