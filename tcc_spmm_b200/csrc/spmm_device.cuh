@@ -294,6 +294,34 @@ __device__ __forceinline__ void mmaTf32TsElected(uint32_t dTmem, uint32_t aTmem,
                  ::"r"(dTmem), "r"(aTmem), "l"(bDesc), "r"(accumulate), "n"(IDESC)
                  : "memory");
 }
+// The 8 MMAs of one full chunk for one 128-feature slice, issued by one elected lane of a warp in
+// uniform control flow: MMA p reads A columns aTmem + ASTEP * p and the B tile at descriptor
+// bDesc + BSTEP * p, all accumulating into dTmem; the first overwrites D unless
+// accumulateFirst != 0. One elect and the operand offsets in one block, so the issuing lane
+// does not rebuild each operand between MMAs.
+template <uint32_t IDESC, uint32_t ASTEP, uint32_t BSTEP>
+__device__ __forceinline__ void mmaTf32Chunk8Elected(uint32_t dTmem, uint32_t aTmem, unsigned long long bDesc,
+                                                     uint32_t accumulateFirst) {
+    asm volatile("{\n\t.reg .pred e, p, t;\n\t.reg .b32 a<8>;\n\t.reg .b64 b<8>;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "setp.ne.b32 p, %3, 0;\n\t"
+                 "setp.ne.b32 t, %4, 0;\n\t"
+                 "add.u32 a1, %1, %6;\n\tadd.u32 a2, a1, %6;\n\tadd.u32 a3, a2, %6;\n\t"
+                 "add.u32 a4, a3, %6;\n\tadd.u32 a5, a4, %6;\n\tadd.u32 a6, a5, %6;\n\tadd.u32 a7, a6, %6;\n\t"
+                 "add.u64 b1, %2, %7;\n\tadd.u64 b2, b1, %7;\n\tadd.u64 b3, b2, %7;\n\t"
+                 "add.u64 b4, b3, %7;\n\tadd.u64 b5, b4, %7;\n\tadd.u64 b6, b5, %7;\n\tadd.u64 b7, b6, %7;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %5, p;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a1], b1, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a2], b2, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a3], b3, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a4], b4, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a5], b5, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a6], b6, %5, t;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a7], b7, %5, t;\n\t}"
+                 ::"r"(dTmem), "r"(aTmem), "l"(bDesc), "r"(accumulateFirst), "r"(1u), "n"(IDESC), "n"(ASTEP),
+                 "n"(static_cast<unsigned long long>(BSTEP))
+                 : "memory");
+}
 // tcgen05.commit issued by one elected lane of a warp in uniform control flow.
 __device__ __forceinline__ void tcCommitElected(uint32_t bar) {
     asm volatile("{\n\t.reg .pred e;\n\t"

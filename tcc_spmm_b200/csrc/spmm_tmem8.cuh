@@ -384,12 +384,9 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 const uint32_t inChunk = min(uint32_t(kChunk8), panelCount - ch * kChunk8);
                 if (inChunk == kChunk8) {
 #pragma unroll
-                    for (uint32_t pp = 0; pp < kChunk8; ++pp)
-#pragma unroll
-                        for (int sl = 0; sl < L::kSlices; ++sl)
-                            dev::mmaTf32TsElected<L::kIdesc>(tmem + sl * L::kSliceCols + 8 * kChunk8,
-                                                             tmem + sl * L::kSliceCols + 8 * pp,
-                                                             desc0 + pp * kTileStep, (ch | pp) != 0);
+                    for (int sl = 0; sl < L::kSlices; ++sl)
+                        dev::mmaTf32Chunk8Elected<L::kIdesc, 8, kTileStep>(
+                            tmem + sl * L::kSliceCols + 8 * kChunk8, tmem + sl * L::kSliceCols, desc0, ch != 0);
                 } else {
                     for (uint32_t pp = 0; pp < inChunk; ++pp)
 #pragma unroll
