@@ -10,10 +10,10 @@
 //
 // The kernels:
 //   spmmTmem8Kernel (spmm_tmem8.cuh): the fast path (tcgen05 MMAs, accumulators in tensor
-//     memory, 8-panel chunks), used when packedX, Y, the partials, sourceIds and
-//     sourceMetadata are 16-byte aligned (always true for cudaMalloc'd buffers).
+//     memory, 8-panel chunks), used when packedX, Y, the partials, sourceIds, sourceMetadata
+//     and values are 16-byte aligned (always true for cudaMalloc'd buffers).
 //   spmmPersistentKernel (spmm_persistent.cuh): mma.sync with register accumulators, when
-//     only the IDs or metadata are not 16-byte aligned.
+//     only the IDs, metadata or values are not 16-byte aligned.
 //   spmmGenericKernel (spmm_generic.cuh): any 2-byte aligned packedX (the reference's own
 //     requirement), operands straight from global memory.
 // Every wait is bounded (about two seconds of %globaltimer); a wait that runs out records a
@@ -147,11 +147,11 @@ void launch(const tcc_sw32_device_view& m, const int8_t* x, const float* scales,
             uint32_t testFlags) {
     const bool fast = aligned(x, 16) && aligned(y, 16) && (partials == nullptr || aligned(partials, 16));
     // Default: the tensor-memory kernel with 8-panel chunks and two producer warps. It moves
-    // the IDs and metadata with bulk copies, which need 16-byte aligned arrays; otherwise the
-    // persistent kernel runs.
+    // the IDs, metadata and value ranges with bulk copies, which need 16-byte aligned arrays;
+    // otherwise the persistent kernel runs.
     if (variant == 0)
         variant = kDefaultVariant;
-    if (variant == 12 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16)))
+    if (variant == 12 && !(aligned(m.sourceIds, 16) && aligned(m.sourceMetadata, 16) && aligned(m.values, 16)))
         variant = F == 128 ? 2 : 3;
     if (variant == 1 || !fast) {
         spmmGenericKernel<F><<<dim3(m.taskCount, F / 128), 128, 0, stream>>>(m, x, scales, y, rows, cols, partials,

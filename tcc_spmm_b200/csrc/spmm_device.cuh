@@ -167,6 +167,20 @@ __device__ __forceinline__ void cpAsync16Line(uint32_t dst, const void* src, uin
     asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(srcBytes)
                  : "memory");
 }
+// cpAsync16Line issued only where id < limit, as one predicated instruction (no branch); the
+// source address is formed but not read where the predicate fails.
+__device__ __forceinline__ void cpAsync16LineIf(uint32_t dst, const void* src, uint32_t id, uint32_t limit) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.lt.u32 p, %2, %3;\n\t"
+                 "@p cp.async.cg.shared.global.L2::128B [%0], [%1], 16;\n\t}" ::"r"(dst),
+                 "l"(src), "r"(id), "r"(limit)
+                 : "memory");
+}
+// A 4-byte cp.async issued only where id < limit (predicated, no branch).
+__device__ __forceinline__ void cpAsync4If(uint32_t dst, const void* src, uint32_t id, uint32_t limit) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.lt.u32 p, %2, %3;\n\t"
+                 "@p cp.async.ca.shared.global [%0], [%1], 4;\n\t}" ::"r"(dst), "l"(src), "r"(id), "r"(limit)
+                 : "memory");
+}
 // 16 zero bytes to shared memory (16-byte aligned address).
 __device__ __forceinline__ void stsZero16(uint32_t addr) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");

@@ -31,10 +31,10 @@
 // Roles (chunks of the CTA's tasks b, b+G, ... form one stream; producer pw owns chunks pw,
 // pw+P, ...):
 //   producers (P warps)  A step (bulk copies of the chunk's 64 IDs and metadata words, kALead
-//                        chunks ahead), V step (kVLead ahead: cp.async of the value range and the
-//                        64 scales, and of the chunk's 64 whole source rows into the shared X ring,
-//                        16 bytes per lane, F / 16 lanes per row), B step (the chunk's 8 B tiles in
-//                        the one shared-memory B buffer).
+//                        chunks ahead), V step (kVLead ahead: one bulk copy of the value range,
+//                        cp.async of the 64 scales and of the chunk's 64 whole source rows into the
+//                        shared X ring, 16 bytes per lane, F / 16 lanes per row), B step (the
+//                        chunk's 8 B tiles in the one shared-memory B buffer).
 //   consumers 0..F/32-1  warp w owns TMEM lane quarter w%4 of slice w/4 (32 features): it reads its
 //                        32 bytes of the chunk's rows from the X ring and stores the A columns. It
 //                        touches no global memory in the chunk loop.
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             dev::mbarInit(barL + 8 * s, 1);
         }
         for (int s = 0; s < L::kVRing; ++s)
-            dev::mbarInit(barV + 8 * s, 32);
+            dev::mbarInit(barV + 8 * s, 33); // the lanes' scale copies and lane 0's value-range copy
         for (int s = 0; s < L::kXDepth; ++s) {
             dev::mbarInit(barXF + 8 * s, 32); // the owning producer's lanes, once their copies land
             dev::mbarInit(barXE + 8 * s, L::kConsumers);
@@ -236,21 +236,21 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                     ok = false;
                     break;
                 }
-                const unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
+                unsigned char* a = smem + L::kAOff + aslot * L::kASlotBytes;
                 unsigned char* v = smem + L::kVOff + vslot * L::kVSlotBytes;
                 const uint32_t np = reinterpret_cast<const uint32_t*>(a + L::kHeaderOff)[1];
                 uint32_t lo = 0xFFFFFFFFu, hi = 0u;
-                uint32_t ids[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const uint32_t slot = lane + 32 * h;
                     const bool inRange = (slot >> 3) < np;
                     const uint32_t id = inRange ? reinterpret_cast<const uint32_t*>(a)[slot] : 0xFFFFFFFFu;
-                    ids[h] = id;
+                    if (!inRange) // past the chunk's last panel: stale, marked invalid for the row copies
+                        reinterpret_cast<uint32_t*>(a)[slot] = 0xFFFFFFFFu;
                     const uint64_t meta =
                         inRange ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
-                    if (id < cols) // an invalid slot's scale is never read (its row mask is empty)
-                        dev::cpAsync4(dev::smemAddr(v + 4 * L::kVCap + 4 * slot), scales + id, 4u);
+                    // an invalid slot's scale is never read (its row mask is empty)
+                    dev::cpAsync4If(dev::smemAddr(v + 4 * L::kVCap + 4 * slot), scales + id, id, cols);
                     const uint32_t mask = static_cast<uint32_t>(meta);
                     const uint32_t first = static_cast<uint32_t>(meta >> 32);
                     if (mask) {
@@ -260,23 +260,40 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 }
                 lo = __reduce_min_sync(0xFFFFFFFFu, lo);
                 hi = __reduce_max_sync(0xFFFFFFFFu, hi);
-                const uint32_t count = hi > lo ? hi - lo : 0u;
-                if (lane == 0)
-                    vBase[vslot] = count <= uint32_t(L::kVCap) ? lo : 0xFFFFFFFFu;
-                if (count <= uint32_t(L::kVCap))
-                    for (uint32_t i = lane; i < count; i += 32)
-                        dev::cpAsync4(dev::smemAddr(v + 4 * i), matrix.values + lo + i, 4);
+                // The value range [lo, hi), widened to 16-byte boundaries, as one bulk copy.
+                const uint32_t lo4 = lo & ~3u;
+                const uint32_t span = hi > lo ? ((hi + 3u) & ~3u) - lo4 : 0u;
+                const bool fits = span <= uint32_t(L::kVCap);
+                if (lane == 0) {
+                    vBase[vslot] = fits ? lo4 : 0xFFFFFFFFu;
+                    if (fits && span != 0) {
+                        dev::fenceProxyAsyncShared(); // earlier generic reads of the slot before the copy
+                        dev::mbarArriveExpectTx(barV + 8 * vslot, 4 * span);
+                        dev::bulkCopyG2S(dev::smemAddr(v), matrix.values + lo4, 4 * span, barV + 8 * vslot);
+                    } else {
+                        dev::mbarArrive(barV + 8 * vslot);
+                    }
+                }
                 dev::cpAsyncArriveNoinc(barV + 8 * vslot);
-                // X rows: whole rows, kLanesPerRow lanes of 16 bytes each; an invalid slot copies
-                // nothing (its A columns keep stale, finite bytes, which meet an all-zero row of B).
-                const uint32_t xdst = base + L::kXOff + xslot * L::kXSlotBytes + 16 * (lane % L::kLanesPerRow);
+                __syncwarp(); // the invalid marks above, before the row copies read the IDs
+                // X rows: whole rows, kLanesPerRow lanes of 16 bytes each. Lane group q copies rows
+                // kGroupRows * q .. + kGroupRows - 1 and reads their IDs four at a time; an invalid
+                // slot copies nothing (its A columns keep stale, finite bytes, which meet an all-zero
+                // row of B).
+                constexpr int kGroupRows = L::kSlots / L::kRowsPerCopy;
+                const uint32_t group = lane / L::kLanesPerRow;
+                const uint32_t xdst = base + L::kXOff + xslot * L::kXSlotBytes + group * kGroupRows * L::kXRowStride +
+                                      16 * (lane % L::kLanesPerRow);
                 const int8_t* xsrc = packedX + 16 * (lane % L::kLanesPerRow);
+                const uint4* gids = reinterpret_cast<const uint4*>(a) + group * (kGroupRows / 4);
 #pragma unroll
-                for (int i = 0; i < L::kSlots / L::kRowsPerCopy; ++i) {
-                    const uint32_t row = L::kRowsPerCopy * i + lane / L::kLanesPerRow;
-                    const uint32_t id = __shfl_sync(0xFFFFFFFFu, ids[(L::kRowsPerCopy * i) >> 5], row & 31);
-                    if (id < cols)
-                        dev::cpAsync16Line(xdst + row * L::kXRowStride, xsrc + uint64_t(id) * F, 16u);
+                for (int i4 = 0; i4 < kGroupRows / 4; ++i4) {
+                    const uint4 q = gids[i4];
+                    const uint32_t id4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        dev::cpAsync16LineIf(xdst + (4 * i4 + k) * L::kXRowStride, xsrc + uint64_t(id4[k]) * F, id4[k],
+                                             cols);
                 }
                 dev::cpAsyncArriveNoinc(barXF + 8 * xslot);
             }
@@ -303,28 +320,37 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
             }
             __syncwarp();
             const uint32_t vb = vBase[vslot];
-            const float* vsm = reinterpret_cast<const float*>(v);
+            // Scatter of the chunk's nonzeros; `fetch(i)` gives value i of a slot's run. The source
+            // of the values (the staged range, or global memory when it did not fit) is chosen
+            // once per chunk, outside the per-nonzero loop.
+            auto scatter = [&](auto fetch) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t slot = lane + 32 * h;
-                const uint32_t pp = slot >> 3, k = slot & 7;
-                const uint64_t meta = pp < np ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
-                const float scale = reinterpret_cast<const float*>(v + 4 * L::kVCap)[slot];
-                uint32_t mask = static_cast<uint32_t>(meta);
-                const uint32_t first = static_cast<uint32_t>(meta >> 32);
-                uint32_t* tile = reinterpret_cast<uint32_t*>(tiles + pp * L::kBTileBytes + (k >> 2) * 128 + (k & 3) * 4);
-                uint32_t j = 0;
-                while (mask) {
-                    const int r = __ffs(mask) - 1;
-                    mask &= mask - 1;
-                    const float value = vb != 0xFFFFFFFFu ? vsm[first + j - vb] : __ldg(matrix.values + first + j);
-                    ++j;
-                    const float b = __uint_as_float(dev::tf32Exact(value)) * scale;
-                    const uint32_t bh = dev::tf32Exact(b);
-                    const uint32_t bl = dev::tf32Exact(b - __uint_as_float(bh));
-                    tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = bh;
-                    tile[((r & 7) * 16 + (r >> 3) * 256 + 1024) / 4] = bl;
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t slot = lane + 32 * h;
+                    const uint32_t pp = slot >> 3, k = slot & 7;
+                    const uint64_t meta =
+                        pp < np ? reinterpret_cast<const uint64_t*>(a + 4 * L::kSlots)[slot] : 0ull;
+                    const float scale = reinterpret_cast<const float*>(v + 4 * L::kVCap)[slot];
+                    uint32_t mask = static_cast<uint32_t>(meta);
+                    uint32_t i = static_cast<uint32_t>(meta >> 32);
+                    uint32_t* tile =
+                        reinterpret_cast<uint32_t*>(tiles + pp * L::kBTileBytes + (k >> 2) * 128 + (k & 3) * 4);
+                    while (mask) {
+                        const int r = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const float b = __uint_as_float(dev::tf32Exact(fetch(i++))) * scale;
+                        const uint32_t bh = dev::tf32Exact(b);
+                        const uint32_t bl = dev::tf32Exact(b - __uint_as_float(bh));
+                        tile[((r & 7) * 16 + (r >> 3) * 256) / 4] = bh;
+                        tile[((r & 7) * 16 + (r >> 3) * 256 + 1024) / 4] = bl;
+                    }
                 }
+            };
+            if (vb != 0xFFFFFFFFu) {
+                const float* vsm = reinterpret_cast<const float*>(v);
+                scatter([&](uint32_t i) { return vsm[i - vb]; });
+            } else {
+                scatter([&](uint32_t i) { return __ldg(matrix.values + i); });
             }
             dev::fenceProxyAsyncShared();
             __syncwarp();
@@ -334,7 +360,11 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
         if (!ok)
             flags[1] = 1;
         dev::cpAsyncWaitAll();
-        // No bulk copy may still be writing into this CTA's shared memory at exit.
+        // No bulk copy may still be writing into this CTA's shared memory at exit: the value
+        // ranges of V steps whose B step did not run (a wait ran out) and the IDs and metadata
+        // of A steps. A phase already waited for returns at once.
+        for (uint32_t s = seqV >= L::kVRing + pw ? seqV - L::kVRing : pw; s < seqV; s += P)
+            boundedWait(barV + 8 * (s % L::kVRing), (s / L::kVRing) & 1);
         for (uint32_t s = seqA >= L::kARing + pw ? seqA - L::kARing : pw; s < seqA; s += P)
             boundedWait(barL + 8 * (s % L::kARing), (s / L::kARing) & 1);
     } else if (warp == L::kMmaWarp) {

@@ -148,6 +148,22 @@ def test_ids_and_metadata_only_4_byte_aligned(features):
     assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, "4-byte aligned IDs/metadata")
 
 
+@pytest.mark.parametrize("features", [128, 256])
+def test_values_only_4_byte_aligned(features):
+    """Values that are not 16-byte aligned (the tensor-memory kernel copies each chunk's value
+    range with one bulk copy) take the kernel without bulk copies; results stay within the
+    bound."""
+    torch = _torch()
+    case = build_case(random_csr(600, 900, 9.0, 6), features, seed=4)
+    vals = torch.empty(case.dm.values.numel() + 1, dtype=torch.float32, device="cuda")[1:]
+    vals.copy_(case.dm.values)
+    case.dm.values = vals
+    y = run_spmm(case)
+    torch.cuda.synchronize()
+    y_ref, bound = oracle_y(case)
+    assert_within_tf32_bound(y.cpu().numpy(), y_ref, bound, "4-byte aligned values")
+
+
 def test_bad_feature_count_raises_invalid_argument():
     torch = _torch()
     case = build_case(random_csr(64, 64, 4.0, 1), 128)
