@@ -273,6 +273,19 @@ int tcc_partition_tasks(const tcc_sw32_task* tasks, uint32_t task_count,
 int tcc_balance_tasks(const tcc_sw32_task* tasks, uint32_t task_count, const uint32_t* row_group_masks,
                       uint32_t features, uint32_t ctas, tcc_sw32_task* out);
 
+/* Task order for one launch of the default kernel, weighted by resident-CTA speed (no reference
+ * counterpart): as tcc_balance_tasks, but the tasks go heaviest first to the CTA that would
+ * finish them earliest, the k-th resident CTA of an SM counting at its measured relative speed
+ * (the SM's schedulers favour older CTAs; CTA b of a full grid of `ctas` CTAs, `ctas_per_sm` per
+ * SM, is the (b / (ctas / ctas_per_sm))-th). CTAs then take different numbers of tasks: CTA b's
+ * list sits at entries b, b + G, ... (G = min(ctas, task_count)), and shorter lists are padded
+ * with entries of window 0xFFFFFFFF (no panels, no rows), which every kernel skips. *out_count
+ * receives the number of entries, G * (longest list); with out == NULL only the count is
+ * returned, else out_capacity must hold it. Y is bit-identical for any such order. */
+int tcc_balance_tasks_padded(const tcc_sw32_task* tasks, uint32_t task_count, const uint32_t* row_group_masks,
+                             uint32_t features, uint32_t ctas, uint32_t ctas_per_sm, tcc_sw32_task* out,
+                             uint64_t out_capacity, uint32_t* out_count);
+
 /* Launch shape of an SpMM kernel variant on the current device (variant 0 = what
  * tcc_launch_spmm_int8 runs on 16-byte aligned arrays): grid (persistent CTAs; 0 for the
  * per-task generic kernel), threads per CTA, dynamic shared memory and resident CTAs per SM. */

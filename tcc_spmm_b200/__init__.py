@@ -6,7 +6,7 @@ include/tcc_spmm_b200.h, C++ drop-in headers beside it). This package mirrors th
 reference's host API in Python for tests and benchmarks.
 """
 from .api import (BUCKET_ORDER, NO_PARTIAL, PADDING_SOURCE, TASK_PANEL_LIMIT, CsrMatrix, CudaError, DeviceMatrix,
-                  UploadedMatrix, balance_tasks,
+                  UploadedMatrix, balance_tasks, balance_tasks_padded,
                   DeviceTimeout, InvalidArgument, MtxMatrix, SpmmWorkspace, Sw32DeviceFormat, Sw32HostFormat,
                   check_device, convert_csr_to_sw32, convert_csr_to_sw32_device, device_status, launch_spmm_int8,
                   load_matrix_market, make_canonical_csr, pack_features_int8x16, partition_tasks,
@@ -21,5 +21,5 @@ __all__ = [
     "load_matrix_market",
     "make_canonical_csr", "pack_features_int8x16", "partition_tasks", "quantize_features_int8",
     "quantize_pack_features_int8", "spmm_launch_shape", "sw32_device_trim", "workspace_size",
-    "library_path", "balance_tasks", "UploadedMatrix",
+    "library_path", "balance_tasks", "balance_tasks_padded", "UploadedMatrix",
 ]

@@ -111,6 +111,8 @@ SIGNATURES = {
     "tcc_sw32_host_free": (None, [C.c_void_p]),
     "tcc_partition_tasks": (C.c_int, [C.c_void_p, C.c_uint32, u32p, C.c_uint32, C.c_uint32, u32p]),
     "tcc_balance_tasks": (C.c_int, [C.c_void_p, C.c_uint32, u32p, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "tcc_balance_tasks_padded": (C.c_int, [C.c_void_p, C.c_uint32, u32p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                           C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32)]),
     "tcc_convert_csr_to_sw32_device": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                                  C.c_uint64, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
     "tcc_sw32_device_sizes": (C.c_int, [C.c_void_p, C.POINTER(Sw32Sizes)]),

@@ -257,6 +257,34 @@ def balance_tasks(tasks: np.ndarray, row_group_masks, features: int, ctas: int) 
     return out
 
 
+def balance_tasks_padded(tasks: np.ndarray, row_group_masks, features: int, ctas: int,
+                         ctas_per_sm: int) -> np.ndarray:
+    """Task order for a persistent launch of `ctas` CTAs, `ctas_per_sm` resident per SM, weighted
+    by the measured speed of each resident CTA (tcc_balance_tasks_padded): CTA b's tasks at
+    entries b, b + G, ...; shorter lists padded with skip entries (window 0xFFFFFFFF). Longer
+    than `tasks` by the padding; Y does not depend on the order."""
+    src = np.ascontiguousarray(tasks)
+    masks = _u32(row_group_masks)
+    n = C.c_uint32()
+    _check(N.lib().tcc_balance_tasks_padded(src.ctypes.data_as(C.c_void_p), src.size, _ptr(masks, C.c_uint32),
+                                            features, ctas, ctas_per_sm, None, 0, C.byref(n)))
+    out = np.empty(n.value, dtype=src.dtype)
+    _check(N.lib().tcc_balance_tasks_padded(src.ctypes.data_as(C.c_void_p), src.size, _ptr(masks, C.c_uint32),
+                                            features, ctas, ctas_per_sm, out.ctypes.data_as(C.c_void_p), out.size,
+                                            C.byref(n)))
+    return out
+
+
+def _balanced_order(tasks: np.ndarray, masks, features: int, variant: str) -> np.ndarray:
+    """The task order a DeviceMatrix launches for `variant` on the current device: weighted by
+    resident-CTA speed and padded for the default kernel, else tcc_balance_tasks's."""
+    shape = spmm_launch_shape(features, variant)
+    if variant in ("default", "tmem8") and shape["grid"]:
+        return balance_tasks_padded(tasks, masks, features, shape["grid"], max(1, shape["occupancy"]))
+    grid = shape["grid"] or spmm_launch_shape(features)["grid"] # the generic kernel's grid is per call
+    return balance_tasks(tasks, masks, features, grid)
+
+
 # --------------------------------------------------------------------------------------------
 # Device side (torch is used for device memory and streams only)
 # --------------------------------------------------------------------------------------------
@@ -318,13 +346,11 @@ class DeviceMatrix:
         tasks = fmt.tasks if task_range is None else fmt.tasks[task_range[0]:task_range[1]]
         self.task_count = int(tasks.size)
         self.tasks = up(np.ascontiguousarray(tasks).view(np.uint32), torch.int32)
-        self.tasks_balanced = None
+        self.tasks_balanced, self.balanced_count = None, 0
         if balance and self.task_count:
             with torch.cuda.device(self.device):
-                # The generic kernel's grid is per call (reported as 0): balance for the default's.
-                grid = spmm_launch_shape(features, variant)["grid"] or spmm_launch_shape(features)["grid"]
-            order = balance_tasks(tasks, fmt.row_group_masks, features, grid)
-            self.tasks_balanced = up(order.view(np.uint32), torch.int32)
+                order = _balanced_order(tasks, fmt.row_group_masks, features, variant)
+            self.tasks_balanced, self.balanced_count = up(order.view(np.uint32), torch.int32), int(order.size)
         self.reductions = up(np.ascontiguousarray(fmt.reductions).view(np.uint32), torch.int32)
         self.partial_ids = up(fmt.partial_ids, torch.int32)
         self.partial_count = fmt.partial_count
@@ -341,12 +367,15 @@ class DeviceMatrix:
         if not 0 <= first <= last <= self.task_count:
             raise ValueError("task range out of bounds")
         whole = first == 0 and last == self.task_count
-        tasks = self.tasks_balanced if (whole and getattr(self, "tasks_balanced", None) is not None) else self.tasks
+        if whole and getattr(self, "tasks_balanced", None) is not None:
+            tasks, count = self.tasks_balanced, self.balanced_count  # with its padding entries
+        else:
+            tasks, count = self.tasks, last - first
         return N.Sw32DeviceView(self.window_offsets.data_ptr(), self.source_ids.data_ptr(),
                                 self.row_group_masks.data_ptr(), self.source_metadata.data_ptr(),
                                 self.values.data_ptr(), self.bucket_offsets.data_ptr(),
-                                tasks.data_ptr() + TASK_DTYPE.itemsize * first, self.reductions.data_ptr(),
-                                self.partial_ids.data_ptr(), last - first)
+                                tasks.data_ptr() + (0 if whole else TASK_DTYPE.itemsize * first),
+                                self.reductions.data_ptr(), self.partial_ids.data_ptr(), count)
 
     @classmethod
     def from_device_format(cls, fmt: "Sw32DeviceFormat", features: int, task_range: Optional[tuple] = None,
@@ -370,14 +399,14 @@ class DeviceMatrix:
         words = TASK_DTYPE.itemsize // 4
         self.tasks = fmt.tasks[words * lo:words * hi] if hi > lo else fmt.tasks[:words]
         self.task_count, self.partial_count = hi - lo, fmt.partial_count
-        self.tasks_balanced = None
+        self.tasks_balanced, self.balanced_count = None, 0
         if balance and self.task_count:
             tasks = host_tasks if host_tasks is not None else fmt.tasks.cpu().numpy().view(np.uint32).view(TASK_DTYPE)
             masks = host_masks if host_masks is not None else fmt.row_group_masks.cpu().numpy().view(np.uint32)
             with torch.cuda.device(self.device):
-                grid = spmm_launch_shape(features, variant)["grid"] or spmm_launch_shape(features)["grid"]
-            order = balance_tasks(tasks[lo:hi], masks, features, grid)
+                order = _balanced_order(tasks[lo:hi], masks, features, variant)
             self.tasks_balanced = torch.from_numpy(order.view(np.uint32).view(np.int32)).to(self.device)
+            self.balanced_count = int(order.size)
         self._format = fmt
         pf, cw = workspace_size(fmt.rows, fmt.partial_count, features)
         self.partials = torch.empty(pf, dtype=torch.float32, device=self.device) if pf else None

@@ -18,6 +18,9 @@ void partitionTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::
                     std::uint32_t features, std::uint32_t parts, std::uint32_t* bounds);
 void balanceTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
                   std::uint32_t features, std::uint32_t ctas, tcc_sw32_task* out);
+std::uint32_t balanceTasksPadded(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
+                                 std::uint32_t features, std::uint32_t ctas, std::uint32_t ctasPerSm,
+                                 tcc_sw32_task* out, std::uint64_t capacity);
 
 namespace {
 thread_local std::string lastError;
@@ -190,6 +193,19 @@ int tcc_balance_tasks(const tcc_sw32_task* tasks, uint32_t task_count, const uin
         if (out == tasks && task_count != 0)
             throw std::invalid_argument("out must not alias tasks");
         tcc::balanceTasks(tasks, task_count, row_group_masks, features, ctas, out);
+    });
+}
+
+int tcc_balance_tasks_padded(const tcc_sw32_task* tasks, uint32_t task_count, const uint32_t* row_group_masks,
+                             uint32_t features, uint32_t ctas, uint32_t ctas_per_sm, tcc_sw32_task* out,
+                             uint64_t out_capacity, uint32_t* out_count) {
+    return tcc::guarded([&] {
+        if (out_count == nullptr)
+            throw std::invalid_argument("out_count must not be null");
+        if (out != nullptr && out == tasks && task_count != 0)
+            throw std::invalid_argument("out must not alias tasks");
+        *out_count = tcc::balanceTasksPadded(tasks, task_count, row_group_masks, features, ctas, ctas_per_sm, out,
+                                             out_capacity);
     });
 }
 

@@ -18,12 +18,14 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <queue>
 
 namespace tcc {
 namespace {
 
 constexpr std::uint32_t kNoPartial = 0xFFFFFFFFu;
 constexpr std::uint32_t kPaddingSource = 0xFFFFFFFFu;
+constexpr std::uint32_t kSkipTaskWindow = 0xFFFFFFFFu; // padding entry of a persistent task order
 
 std::uint32_t to32(std::uint64_t n) {
     if (n > std::numeric_limits<std::uint32_t>::max())
@@ -465,6 +467,97 @@ void balanceTasks(const tcc_sw32_task* tasks, std::uint32_t count, const std::ui
         for (std::size_t k = 0; k < list.size(); ++k)
             out[b + k * g] = tasks[list[k]];
     }
+}
+
+// Relative speed of the k-th resident CTA of an SM (k = b / (G / ctasPerSm) for CTA b of a
+// full persistent grid of G CTAs, which the hardware makes resident in block order), measured
+// on B200 for the tensor-memory kernel: the SM's schedulers favour the older CTAs' warps, so
+// with equal work the fourth CTA of an SM takes 15% longer than the first (power-law and R-MAT
+// alike); the speeds below are those seen once the work is dealt by them (power-law, stress).
+// Other residencies get equal speeds.
+double residentSpeed(std::uint32_t ctasPerSm, std::uint32_t k) {
+    static const double four[4] = {1.0, 0.94, 0.90, 0.82};
+    static const double two[2] = {1.0, 0.895};
+    if (ctasPerSm == 4 && k < 4)
+        return four[k];
+    if (ctasPerSm == 2 && k < 2)
+        return two[k];
+    return 1.0;
+}
+
+// Task order for a persistent launch in which CTA b takes entries b, b + G, b + 2G, ... and
+// CTAs run at the speeds of residentSpeed: tasks dealt heaviest first, each to the CTA that
+// would finish it earliest (longest-processing-time on machines of different speeds), so the
+// CTAs receive different numbers of tasks. CTA b's list is laid out at b + k * G; shorter lists
+// are padded with entries of window kSkipTask (no panels, no rows) that every kernel skips.
+// Returns the number of entries, G * (longest list); `out` may be null to query it.
+std::uint32_t balanceTasksPadded(const tcc_sw32_task* tasks, std::uint32_t count, const std::uint32_t* masks,
+                                 std::uint32_t features, std::uint32_t ctas, std::uint32_t ctasPerSm,
+                                 tcc_sw32_task* out, std::uint64_t capacity) {
+    if (ctas == 0 || ctasPerSm == 0 || (count != 0 && tasks == nullptr))
+        throw std::invalid_argument("invalid task balance request");
+    if (count == 0)
+        return 0;
+    const std::uint32_t g = std::min(ctas, count);
+    const bool full = g == ctas && ctas % ctasPerSm == 0;
+    const std::uint32_t perRank = full ? ctas / ctasPerSm : g;
+    std::vector<double> cost(count);
+    for (std::uint32_t i = 0; i < count; ++i)
+        cost[i] = taskCost(tasks[i], masks, features);
+    std::vector<std::uint32_t> order(count);
+    for (std::uint32_t i = 0; i < count; ++i)
+        order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](std::uint32_t a, std::uint32_t b) { return cost[a] > cost[b]; });
+    // One min-heap of (load, CTA) per speed class: the earliest finish of a task is at the top of
+    // one of them.
+    const std::uint32_t classes = full ? ctasPerSm : 1;
+    using Entry = std::pair<double, std::uint32_t>;
+    std::vector<std::priority_queue<Entry, std::vector<Entry>, std::greater<Entry>>> heaps(classes);
+    std::vector<double> speed(classes);
+    for (std::uint32_t c = 0; c < classes; ++c)
+        speed[c] = full ? residentSpeed(ctasPerSm, c) : 1.0;
+    // The last kBoundary CTAs before each residency boundary are sometimes made resident after
+    // the first ones of the next rank: deal them at the slower speed.
+    constexpr std::uint32_t kBoundary = 12;
+    for (std::uint32_t b = 0; b < g; ++b) {
+        std::uint32_t c = full ? b / perRank : 0;
+        if (full && c + 1 < classes && b % perRank >= perRank - std::min(kBoundary, perRank / 4))
+            ++c;
+        heaps[c].push({0.0, b});
+    }
+    std::vector<std::vector<std::uint32_t>> lists(g);
+    for (std::uint32_t at = 0; at < count; ++at) {
+        const std::uint32_t task = order[at];
+        std::uint32_t best = 0;
+        double bestFinish = 0.0;
+        for (std::uint32_t c = 0; c < classes; ++c) {
+            const double finish = (heaps[c].top().first + cost[task]) / speed[c];
+            if (c == 0 || finish < bestFinish) {
+                best = c;
+                bestFinish = finish;
+            }
+        }
+        Entry e = heaps[best].top();
+        heaps[best].pop();
+        lists[e.second].push_back(task);
+        e.first += cost[task];
+        heaps[best].push(e);
+    }
+    std::size_t longest = 0;
+    for (const auto& l : lists)
+        longest = std::max(longest, l.size());
+    const std::uint64_t entries = std::uint64_t(g) * longest;
+    if (entries > 0xFFFFFFFFull)
+        throw std::invalid_argument("padded task order too long");
+    if (out == nullptr)
+        return static_cast<std::uint32_t>(entries);
+    if (capacity < entries)
+        throw std::invalid_argument("output capacity below the padded task count");
+    const tcc_sw32_task skip{kSkipTaskWindow, 0, 0, kNoPartial, 0, 0, 0};
+    for (std::uint32_t b = 0; b < g; ++b)
+        for (std::size_t k = 0; k < longest; ++k)
+            out[b + k * g] = k < lists[b].size() ? tasks[lists[b][k]] : skip;
+    return static_cast<std::uint32_t>(entries);
 }
 
 } // namespace tcc

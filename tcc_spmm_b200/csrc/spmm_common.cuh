@@ -12,6 +12,9 @@ __device__ unsigned int gDeviceStatus = 0;
 
 namespace {
 constexpr uint32_t kNoPartial = 0xFFFFFFFFu;
+// Window index of a padding entry in a task order built for a persistent grid
+// (tcc_balance_tasks_padded): it has no panels and no rows, and every kernel skips it.
+constexpr uint32_t kSkipTask = 0xFFFFFFFFu;
 constexpr uint64_t kWaitLimitNs = 2000000000ull; // about two seconds per wait
 
 // Wait for the given phase of an mbarrier. The warp is suspended by the hardware between

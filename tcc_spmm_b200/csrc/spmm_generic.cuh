@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(128) spmmGenericKernel(const tcc_sw32_device_v
         }
     }
     // Fragment (part, i): feature featureBase + 16*part + g + 8*(i>=2), row 8rw + 2t + (i&1).
+    if (task.sw == kSkipTask) // a padding entry: no panels, no rows
+        return;
     const uint32_t rowBase = task.sw * 32;
     if (task.partial != kNoPartial && (partials == nullptr || counters == nullptr)) {
         if (threadIdx.x == 0) // split tasks need the workspace

@@ -431,6 +431,8 @@ __global__ void __launch_bounds__(Persist<F, FPW, P>::kThreads)
                     dev::mbarArrive(barE + 8 * stage);
             }
             // ---- write-back of this task ----
+            if (task.sw == kSkipTask) // a padding entry: no panels, no rows
+                continue;
             const uint32_t rowBase = task.sw * 32;
             const bool split = task.partial != kNoPartial;
             if (split && (partials == nullptr || counters == nullptr)) {

@@ -500,6 +500,8 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 dev::mbarArriveIf(lane == 0, barXE + 8 * xslot); // the chunk's X rows are read
             }
             // ---- epilogue of this window ----
+            if (task.sw == kSkipTask) // a padding entry: no panels (no chunks above), no rows
+                continue;
             const uint32_t rowBase = task.sw * 32;
             const bool split = task.partial != kNoPartial;
             const bool haveWs = !split || (partials != nullptr && counters != nullptr);

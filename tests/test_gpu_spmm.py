@@ -212,17 +212,21 @@ def test_matches_reference_kernel(name, tag, features):
 
 @pytest.mark.parametrize("features", [128, 256])
 @pytest.mark.parametrize("name", ["stress_small", "powerlaw_small"])
-def test_balanced_task_order_bit_identical(name, features):
-    """Y does not depend on the task order: the balanced order of tcc_balance_tasks gives the
-    same bits as the format order (split windows merge their partials in a fixed order)."""
+@pytest.mark.parametrize("variant", ["default", "generic", "persistent32", "persistent64"])
+def test_balanced_task_order_bit_identical(name, features, variant):
+    """Y does not depend on the task order: the speed-weighted order with its skip entries
+    (tcc_balance_tasks_padded, what a balanced DeviceMatrix launches) gives the same bits as the
+    format order in every kernel, which all skip the padding (split windows merge their
+    partials in a fixed order)."""
     torch = _torch()
     case = build_case(W.generate(name), features, seed=17)
-    y = run_spmm(case)
+    y = run_spmm(case, variant=variant)
     balanced = T.DeviceMatrix(case.fmt, features, "cuda", balance=True)
     assert balanced.tasks_balanced is not None
+    assert balanced.balanced_count > case.fmt.tasks.size, "the order has skip entries"
     y2 = torch.full_like(y, float("nan"))
     T.launch_spmm_int8(balanced.view(), case.packed_dev, case.scales_dev, y2, case.fmt.rows, case.fmt.cols,
-                       features, balanced.workspace())
+                       features, balanced.workspace(), variant=variant)
     torch.cuda.synchronize()
     assert torch.equal(y.view(torch.int32), y2.view(torch.int32))
     assert int(balanced.counters.abs().sum()) == 0
