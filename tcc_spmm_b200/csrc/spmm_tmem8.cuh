@@ -260,20 +260,25 @@ __global__ void __launch_bounds__(Tmem8<F, P>::kThreads, Tmem8<F, P>::kMaxCtasPe
                 }
                 lo = __reduce_min_sync(0xFFFFFFFFu, lo);
                 hi = __reduce_max_sync(0xFFFFFFFFu, hi);
-                // The value range [lo, hi), widened to 16-byte boundaries, as one bulk copy.
+                // The value range [lo, hi) from the 16-byte boundary at or below lo: its whole
+                // 16-byte groups as one bulk copy, the last 0-3 values (which never reach past hi,
+                // the end of the chunk's values) by cp.async.
                 const uint32_t lo4 = lo & ~3u;
-                const uint32_t span = hi > lo ? ((hi + 3u) & ~3u) - lo4 : 0u;
+                const uint32_t span = hi > lo ? hi - lo4 : 0u;
+                const uint32_t bulk = span & ~3u;
                 const bool fits = span <= uint32_t(L::kVCap);
                 if (lane == 0) {
                     vBase[vslot] = fits ? lo4 : 0xFFFFFFFFu;
-                    if (fits && span != 0) {
+                    if (fits && bulk != 0) {
                         dev::fenceProxyAsyncShared(); // earlier generic reads of the slot before the copy
-                        dev::mbarArriveExpectTx(barV + 8 * vslot, 4 * span);
-                        dev::bulkCopyG2S(dev::smemAddr(v), matrix.values + lo4, 4 * span, barV + 8 * vslot);
+                        dev::mbarArriveExpectTx(barV + 8 * vslot, 4 * bulk);
+                        dev::bulkCopyG2S(dev::smemAddr(v), matrix.values + lo4, 4 * bulk, barV + 8 * vslot);
                     } else {
                         dev::mbarArrive(barV + 8 * vslot);
                     }
                 }
+                if (fits && lane < span - bulk)
+                    dev::cpAsync4(dev::smemAddr(v + 4 * (bulk + lane)), matrix.values + lo4 + bulk + lane, 4u);
                 dev::cpAsyncArriveNoinc(barV + 8 * vslot);
                 __syncwarp(); // the invalid marks above, before the row copies read the IDs
                 // X rows: whole rows, kLanesPerRow lanes of 16 bytes each. Lane group q copies rows
