@@ -74,6 +74,9 @@ def parse_args():
     p.add_argument("--no-assembly", action="store_true", help="skip the optional Y assembly across ranks")
     p.add_argument("--natural-order", action="store_true",
                    help="launch the tasks in format order instead of the balanced order (tcc_balance_tasks)")
+    p.add_argument("--equal-count-order", action="store_true",
+                   help="balanced order with equal task counts per CTA (tcc_balance_tasks) instead of the one "
+                        "weighted by resident-CTA speed (tcc_balance_tasks_padded)")
     p.add_argument("--variant", default="default", choices=["default", "generic", "persistent32", "persistent64", "tmem8"],
                    help="SpMM kernel (default: what launchSpmmInt8 runs)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -243,9 +246,10 @@ class DeviceWorkload:
                            lambda p0, p1: int((self.dfmt.source_ids[8 * p0:8 * p1] != -1).sum().item()),
                            lambda r0, r1: int(ro[r1].item()) - int(ro[r0].item()))
 
-    def device_matrix(self, features: int, task_range, balance: bool, variant: str):
+    def device_matrix(self, features: int, task_range, balance: bool, variant: str, weighted: bool = True):
         return self.dfmt.device_matrix(features, task_range=task_range, balance=balance, variant=variant,
-                                       host_tasks=self.tasks, host_masks=self.row_group_masks)
+                                       host_tasks=self.tasks, host_masks=self.row_group_masks,
+                                       weighted_order=weighted)
 
 
 def device_inputs(T, cols: int, features: int, device, seed: int = X_SEED):
@@ -537,7 +541,7 @@ def run_tcc(args):
     threads = max(1, host_threads() // world)
     stream = torch.cuda.current_stream(device)
     peak, peak_kind = measured_peaks()
-    task_order = "format" if args.natural_order else "balanced"
+    task_order = "format" if args.natural_order else "balanced-equal" if args.equal_count_order else "balanced"
 
     def barrier():
         if world > 1:
@@ -555,7 +559,7 @@ def run_tcc(args):
     lo, hi = int(bounds[rank]), int(bounds[rank + 1])
     shard = wl.bytes(lo, hi, F)
     full = wl.bytes(0, wl.tasks.size, F)
-    dm = wl.device_matrix(F, (lo, hi), not args.natural_order, args.variant)
+    dm = wl.device_matrix(F, (lo, hi), not args.natural_order, args.variant, not args.equal_count_order)
     x, packed, scales = device_inputs(T, wl.cols, F, device)
     y = torch.empty((wl.rows, F), device=device)
     view, ws = dm.view(), dm.workspace()
@@ -648,7 +652,8 @@ def run_tcc(args):
         "config": headline_config,
         "parallelism": f"task-range shards x{world}, X replicated, Y rows per rank",
         "kernel": {"variant": args.variant, "task_order": "format order" if args.natural_order else
-                   "balanced for the launch grid", "launch": shape},
+                   "balanced for the launch grid, equal task counts per CTA" if args.equal_count_order else
+                   "balanced for the launch grid, weighted by resident-CTA speed", "launch": shape},
         "prep": headline_prep,
         "timing": {"method": "K launches between CUDA events on the launching stream, barrier + synchronize on "
                              "both sides, max over ranks; also split into 5 event-timed batches",
@@ -676,7 +681,7 @@ def run_config(args, T, W, name, reuse, device, stream, world, rank, threads, ba
     lo, hi = int(bounds[rank]), int(bounds[rank + 1])
     shard = wl.bytes(lo, hi, F)
     full = wl.bytes(0, wl.tasks.size, F)
-    dm = wl.device_matrix(F, (lo, hi), not args.natural_order, args.variant)
+    dm = wl.device_matrix(F, (lo, hi), not args.natural_order, args.variant, not args.equal_count_order)
     x, packed, scales = device_inputs(T, wl.cols, F, device, seed=X_SEED + 1)
     del x
     y = torch.empty((wl.rows, F), device=device)

@@ -275,11 +275,12 @@ def balance_tasks_padded(tasks: np.ndarray, row_group_masks, features: int, ctas
     return out
 
 
-def _balanced_order(tasks: np.ndarray, masks, features: int, variant: str) -> np.ndarray:
+def _balanced_order(tasks: np.ndarray, masks, features: int, variant: str, weighted: bool = True) -> np.ndarray:
     """The task order a DeviceMatrix launches for `variant` on the current device: weighted by
-    resident-CTA speed and padded for the default kernel, else tcc_balance_tasks's."""
+    resident-CTA speed and padded for the default kernel (unless weighted is False), else
+    tcc_balance_tasks's equal-count order."""
     shape = spmm_launch_shape(features, variant)
-    if variant in ("default", "tmem8") and shape["grid"]:
+    if weighted and variant in ("default", "tmem8") and shape["grid"]:
         return balance_tasks_padded(tasks, masks, features, shape["grid"], max(1, shape["occupancy"]))
     grid = shape["grid"] or spmm_launch_shape(features)["grid"] # the generic kernel's grid is per call
     return balance_tasks(tasks, masks, features, grid)
@@ -326,7 +327,7 @@ class DeviceMatrix:
     contiguous windows)."""
 
     def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None,
-                 balance: bool = False, variant: str = "default"):
+                 balance: bool = False, variant: str = "default", weighted_order: bool = True):
         import torch
 
         self.rows, self.cols, self.features = fmt.rows, fmt.cols, features
@@ -349,7 +350,7 @@ class DeviceMatrix:
         self.tasks_balanced, self.balanced_count = None, 0
         if balance and self.task_count:
             with torch.cuda.device(self.device):
-                order = _balanced_order(tasks, fmt.row_group_masks, features, variant)
+                order = _balanced_order(tasks, fmt.row_group_masks, features, variant, weighted_order)
             self.tasks_balanced, self.balanced_count = up(order.view(np.uint32), torch.int32), int(order.size)
         self.reductions = up(np.ascontiguousarray(fmt.reductions).view(np.uint32), torch.int32)
         self.partial_ids = up(fmt.partial_ids, torch.int32)
@@ -380,7 +381,7 @@ class DeviceMatrix:
     @classmethod
     def from_device_format(cls, fmt: "Sw32DeviceFormat", features: int, task_range: Optional[tuple] = None,
                            balance: bool = False, variant: str = "default", host_tasks: Optional[np.ndarray] = None,
-                           host_masks: Optional[np.ndarray] = None) -> "DeviceMatrix":
+                           host_masks: Optional[np.ndarray] = None, weighted_order: bool = True) -> "DeviceMatrix":
         """A DeviceMatrix over a format built on the GPU (no upload): the arrays are the
         library's; only the workspace for `features` is allocated here. task_range and balance
         as in the constructor; balancing reads the tasks and row-group masks on the host
@@ -404,7 +405,7 @@ class DeviceMatrix:
             tasks = host_tasks if host_tasks is not None else fmt.tasks.cpu().numpy().view(np.uint32).view(TASK_DTYPE)
             masks = host_masks if host_masks is not None else fmt.row_group_masks.cpu().numpy().view(np.uint32)
             with torch.cuda.device(self.device):
-                order = _balanced_order(tasks[lo:hi], masks, features, variant)
+                order = _balanced_order(tasks[lo:hi], masks, features, variant, weighted_order)
             self.tasks_balanced = torch.from_numpy(order.view(np.uint32).view(np.int32)).to(self.device)
             self.balanced_count = int(order.size)
         self._format = fmt
