@@ -321,10 +321,12 @@ class DeviceMatrix:
     (reference src/device_matrix.cuh:8-37): partials = partialCount*8*F floats, counters =
     windows*(F/128) zeroed u32 when partialCount > 0.
 
-    balance=True also uploads the tasks in the order of balance_tasks for the grid of the
-    kernel `variant` (the default kernel unless named) on this device; view() of the whole task
-    range then uses that order (sub-range views keep the natural order, whose ranges cover
-    contiguous windows)."""
+    balance=True also uploads a task order for the grid of the kernel `variant` (the default
+    kernel unless named) on this device: for the default kernel the order weighted by the speed
+    of each resident CTA of an SM, padded with skip entries (balance_tasks_padded), or with
+    weighted_order=False, and for the other kernels, the equal-count order of balance_tasks.
+    view() of the whole task range then uses that order (sub-range views keep the natural order,
+    whose ranges cover contiguous windows)."""
 
     def __init__(self, fmt: Sw32HostFormat, features: int, device="cuda", task_range: Optional[tuple] = None,
                  balance: bool = False, variant: str = "default", weighted_order: bool = True):
