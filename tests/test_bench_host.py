@@ -84,7 +84,18 @@ def test_traffic_entry_matches_launch_shape():
     other = dict(same, smem=same["smem"] + 128)
     assert bench.profile_traffic("powerlaw128", "default", "balanced", other) is None
     assert bench.profile_traffic("powerlaw128", "default", "format") is None
+    assert bench.profile_traffic("powerlaw128", "default", "balanced-equal") is None  # another task order
     assert bench.profile_traffic("powerlaw128", "generic", "balanced") is None
+
+
+def test_task_order_flags(monkeypatch):
+    """The weighted task order is the default; --equal-count-order and --natural-order select
+    the others."""
+    monkeypatch.setattr("sys.argv", ["bench.py"])
+    args = bench.parse_args()
+    assert not args.equal_count_order and not args.natural_order
+    monkeypatch.setattr("sys.argv", ["bench.py", "--equal-count-order"])
+    assert bench.parse_args().equal_count_order
 
 
 @pytest.mark.parametrize("cols,world", [(1, 2), (7, 2), (8, 4), (2_449_029, 4), (5, 8), (100, 3)])
